@@ -1,0 +1,306 @@
+"""Headline benchmark: Engram fetch GB/s per requester and fetch->hook latency.
+
+Workload (the reference's headline shape, ``README.md:123,130`` and
+``benchmarks/test_read.py:19-20,288-291``): FP8 e4m3 rows of hidden=256 with
+two 128-column fp32 scale packs, 2 layers of 524288 / 524309 rows per rank,
+4096 tokens x 24 entries per token per requester, uniform requests over all
+``world * n`` global rows, random-init weights (N(0,1) e4m3 codes with
+power-of-two scales).  Every rank is a requester and an owner ("all-to-all"
+traffic).
+
+One step = ``fetch(indices)`` plus every layer hook, i.e. the full lookup
+(issue + transfer + scales) as the reference times it.  Each timed step uses a
+fresh index tensor and the L2 is flushed (256 MiB write) between steps outside
+the timed events.  Times are CUDA events on the launching stream; the reported
+step time is the maximum over ranks.
+
+Run: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
+``torchrun --nproc-per-node N``.  ``--impl nccl`` times the torch
+``all_to_all`` baseline; ``--impl reference`` reports the reference build.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_GBS_PER_REQUESTER = 180.0  # upper end of the reference's published 175-180 GB/s/requester
+METRIC = "Engram fetch GB/s/requester and p50 fetch→hook latency, 8×B200, 4096 tok"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "nccl", "reference"], default="ours")
+    p.add_argument("--config", default="fp8", help="table set from engram_rdma_lab_b200.models.CONFIGS")
+    p.add_argument("--tokens", type=int, default=None)
+    p.add_argument("--route", choices=["peer_hbm", "host"], default="peer_hbm",
+                   help="peer_hbm: ENGRAM_EGM_ENABLE=1 (HBM mirror, NVLink pull); host: owner push from host shards")
+    p.add_argument("--distribution", default=None)
+    p.add_argument("--graph", action="store_true", help="replay fetch+hooks from a CUDA graph")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-clocks", action="store_true")
+    return p.parse_args()
+
+
+def unavailable_reference():
+    reason = (
+        "reference cannot be built or run on this box: deep_ep needs an NCCL with the GIN/GDAKI device API "
+        "(NCCL 2.28.9 here) and fails to compile against CUDA 12.9; engram_sge_write needs NCCL_ROOT with GIN "
+        "plus ibverbs/mlx5 HCAs; both need 2 nodes x 4 GPUs with RDMA NICs"
+    )
+    print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+def init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if world == 1:
+            import socket
+
+            with socket.socket() as s:
+                s.bind(("127.0.0.1", 0))
+                os.environ.setdefault("MASTER_PORT", str(s.getsockname()[1]))
+        import datetime
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def build_buffer(args, spec, rank, world):
+    from engram_rdma_lab_b200 import EngramBuffer, TorchEngramBuffer
+    from engram_rdma_lab_b200.models import quantized_fp8_shard, normal_bf16_shard
+
+    os.environ["ENGRAM_EGM_ENABLE"] = "1" if args.route == "peer_hbm" else "0"
+    os.environ.setdefault("ENGRAM_WRITE_LOCAL_SF", "1")
+    cls = EngramBuffer if args.impl == "ours" else TorchEngramBuffer
+    group = dist.group.WORLD
+    sizes = cls.get_storage_size_hint(group, spec.entries, spec.hidden, spec.max_tokens, spec.ept, spec.dtype,
+                                      spec.num_sf_packs)
+    cfg = cls.get_theoretical_config(group, spec.layers, spec.max_tokens, spec.ept)
+    buf = cls(group, *sizes, True, *cfg, num_gpu_timeout_secs=60, explicitly_destroy=True)
+    buf.set_config(spec.entries, spec.hidden, spec.max_tokens, spec.ept, spec.dtype, spec.num_sf_packs)
+    if spec.num_sf_packs:
+        storages, scales = quantized_fp8_shard(rank, world, spec.entries, spec.hidden, spec.num_sf_packs, "cuda")
+    else:
+        storages, scales = normal_bf16_shard(rank, world, spec.entries, spec.hidden, "cuda"), None
+    buf.write(storages, scales)
+    del storages, scales
+    torch.cuda.empty_cache()
+    return buf
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            unavailable_reference()
+        return
+    rank, world, local = init()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    from engram_rdma_lab_b200.models import CONFIGS, make_indices
+    from engram_rdma_lab_b200.parallel import gather_floats
+    from engram_rdma_lab_b200.utils.timing import ClockSampler, L2Flusher, percentile
+
+    spec = CONFIGS[args.config]
+    if args.tokens:
+        spec = spec.with_(tokens=args.tokens, max_tokens=max(spec.max_tokens, args.tokens))
+    if args.distribution:
+        spec = spec.with_(distribution=args.distribution)
+    T = spec.tokens
+    buf = build_buffer(args, spec, rank, world)
+    pool_size = max(2, min(args.steps, 16))
+    pool = [make_indices(rank, world, spec.entries, T, spec.ept, epoch=e + 1, distribution=spec.distribution,
+                         padding=spec.padding, device="cuda") for e in range(pool_size)]
+    flush = L2Flusher()
+    stream = torch.cuda.current_stream()
+    native = args.impl == "ours"
+
+    def step(idx):
+        hooks = buf.fetch(idx)
+        return [h() for h in hooks]
+
+    graph, graph_idx = None, None
+    if args.graph:
+        graph_idx = pool[0].clone()
+        for _ in range(2):
+            step(graph_idx)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(graph_idx)
+
+    def run(k):
+        if graph is None:
+            return step(pool[k % pool_size])
+        graph_idx.copy_(pool[k % pool_size])
+        graph.replay()
+        return None
+
+    for k in range(args.warmup):
+        run(k)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches_before = buf.runtime.memory_usage()["kernel_launches"] if native else 0
+    sampler = ClockSampler(gpu_index=_physical_index(local)) if not args.no_clocks else None
+    if sampler:
+        sampler.__enter__()
+    dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for k in range(args.steps):
+        flush()
+        if graph is not None:
+            graph_idx.copy_(pool[k % pool_size])
+        starts[k].record(stream)
+        if graph is None:
+            step(pool[k % pool_size])
+        else:
+            graph.replay()
+        ends[k].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    dist.barrier()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    launches = (buf.runtime.memory_usage()["kernel_launches"] - launches_before) if native else 0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    all_ms = gather_floats(step_ms)
+    per_step_max = [max(r[k] for r in all_ms) for k in range(args.steps)]
+    rank_totals = [sum(r) for r in all_ms]
+    ms_per_step = max(rank_totals) / args.steps
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(buf, spec, pool, flush, args, rank, world, graph is not None)
+
+    clocks = sampler.summary() if sampler else {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["not sampled"]}
+    all_clocks = [None] * world
+    dist.all_gather_object(all_clocks, clocks)
+    if rank == 0:
+        bytes_req = spec.bytes_per_fetch(T)
+        per_req_gbs = bytes_req / (ms_per_step * 1e-3) / 1e9
+        reasons = sorted({r for c in all_clocks for r in (c.get("reasons") or [])})
+        line = {
+            "metric": METRIC,
+            "value": round(per_req_gbs * world, 3),
+            "unit": "GB/s (sum over requesters)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(per_req_gbs / BASELINE_GBS_PER_REQUESTER, 3),
+            "dtype": "fp8_e4m3" if spec.num_sf_packs else "bf16",
+            "data": "synthetic (random-init tables, seeded uniform indices)",
+            "impl": "ours" if native else "nccl_all_to_all_baseline",
+            "per_requester_gbs": round(per_req_gbs, 3),
+            "p50_fetch_to_hook_us": round(statistics.median(per_step_max) * 1e3, 2),
+            "p99_fetch_to_hook_us": round(percentile(per_step_max, 0.99) * 1e3, 2),
+            "gpu_launches": int(launches),
+            "wall_s_timed_loop": round(wall, 3),
+            "e2e": e2e,
+            "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"), "reasons": reasons,
+                       "per_rank_sm_mhz": [c.get("sm_mhz") for c in all_clocks]},
+            "config": {
+                "model": f"engram {spec.name}: {spec.layers} layers x {list(spec.entries)} rows/rank, hidden "
+                         f"{spec.hidden}, ept {spec.ept}, {spec.num_sf_packs} scale packs",
+                "global_batch": T * world,
+                "seq_len": T,
+                "tokens_per_requester": T,
+                "bytes_per_requester_per_step": bytes_req,
+                "parallelism": f"vocab-sharded x{world} (every rank requester and owner)",
+                "route": args.route if native else "all_to_all",
+                "graph": bool(args.graph),
+                "distribution": spec.distribution,
+                "l2": "flushed between timed steps (256 MiB write outside the events); fresh indices per step",
+                "timing": "CUDA events per step on the launching stream, max over ranks",
+                "baseline_gbs_per_requester": BASELINE_GBS_PER_REQUESTER,
+            },
+        }
+        print(json.dumps(line), flush=True)
+    buf.destroy()
+    del graph
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
+    """Same metric through the public API with the input H2D and a result D2H per step."""
+    stream = torch.cuda.current_stream()
+    host_pool = [p.cpu().pin_memory() for p in pool[: min(len(pool), 8)]]
+    dev_idx = torch.empty_like(pool[0])
+    packs = spec.num_sf_packs
+    out_host = torch.empty(spec.layers, spec.ept * spec.row_bytes, dtype=torch.uint8).pin_memory()
+    sf_host = torch.empty(spec.layers, max(1, spec.ept * packs), dtype=torch.float32).pin_memory()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for k in range(args.warmup + args.steps):
+        timed = k >= args.warmup
+        flush()
+        if timed:
+            starts[k - args.warmup].record(stream)
+        dev_idx.copy_(host_pool[k % len(host_pool)], non_blocking=True)
+        outs = [h() for h in buf.fetch(dev_idx)]
+        for layer, out in enumerate(outs):
+            data, sf = out if packs else (out, None)
+            if data.shape[0]:
+                out_host[layer].copy_(data[0].view(torch.uint8), non_blocking=True)
+                if packs:
+                    sf_host[layer].copy_(sf[0], non_blocking=True)
+        if timed:
+            ends[k - args.warmup].record(stream)
+    torch.cuda.synchronize()
+    from engram_rdma_lab_b200.parallel import gather_floats
+
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    totals = [sum(r) for r in gather_floats(ms)]
+    ms_per_step = max(totals) / args.steps
+    bytes_req = spec.bytes_per_fetch(pool[0].shape[1])
+    per_req = bytes_req / (ms_per_step * 1e-3) / 1e9
+    return {
+        "value": round(per_req * world, 3),
+        "unit": "GB/s (sum over requesters)",
+        "per_requester_gbs": round(per_req, 3),
+        "ms_per_step": round(ms_per_step, 5),
+        "h2d_bytes_per_step": int(pool[0].numel() * pool[0].element_size()),
+        "d2h_bytes_per_step": int(spec.layers * (spec.ept * spec.row_bytes + (spec.ept * packs * 4 if packs else 0))),
+        "path": "pinned H2D of indices -> fetch -> hooks -> D2H of token 0's rows and scales, per step",
+        "graph": False if not use_graph else "eager API (graph used only for the device-timed value)",
+    }
+
+
+def _physical_index(local):
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        items = [v.strip() for v in visible.split(",") if v.strip()]
+        if local < len(items) and items[local].isdigit():
+            return int(items[local])
+        return None
+    return local
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,141 @@
+// Launch parameters of the Engram kernels.  Plain structs passed by value, so
+// CUDA Graph capture records them in the kernel node and replays never need a
+// device-side metadata table.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace engram {
+
+constexpr int kMaxRanks = 64;
+constexpr int kMaxLayers = 32;
+constexpr int kHeaderBytes = 64;
+constexpr int kMaxPushTasks = 64;
+
+// Error record shared with the host through mapped pinned memory.  The first
+// failing thread wins; later failures only bump the count.
+struct ErrorRecord {
+    uint32_t status;   // 0 = healthy, else one of ErrorCode
+    uint32_t layer;
+    uint32_t owner;
+    uint32_t count;
+    uint64_t observed;
+    uint64_t expected;
+};
+
+// Where kernels report errors: atomics go to a device-resident record (atomics
+// on mapped host memory are not guaranteed over PCIe); the winning thread then
+// mirrors its report into host-mapped memory with plain system-scope stores,
+// status last, so the host can poll it without synchronising the stream.
+struct ErrorSink {
+    ErrorRecord *dev;
+    ErrorRecord *host;
+};
+
+enum ErrorCode : uint32_t {
+    kOk = 0,
+    kWaitTimeout = 1,      // hook gave up waiting for an owner's done flag
+    kIndexOutOfRange = 2,  // a request named a row beyond the global vocabulary
+    kInboxOverflow = 3,    // a request list exceeded the inbox slot
+    kPushBounds = 4,       // an owner got a row id or position out of bounds
+};
+
+
+// Mailbox header written by a requester's GPU into the owner's host shard and
+// polled by the owner's service thread.  One slot per [requester][layer].
+struct alignas(64) MailboxHeader {
+    uint64_t ready;     // request epoch, published last with st.release.sys
+    uint32_t rows;      // number of (row, position) entries in the inbox slot
+    uint32_t layer;
+    uint32_t requester;
+    uint32_t channels;  // push CTAs the requester asks for (its num_qps)
+    uint32_t reserved[10];
+};
+static_assert(sizeof(MailboxHeader) == kHeaderBytes, "mailbox header ABI");
+
+// Per-layer geometry shared by all kernels.
+struct LayerTable {
+    uint32_t entries[kMaxLayers];      // rows per rank (n_l)
+    uint32_t table_bases[kMaxLayers];  // first local row of layer l in a shard
+    uint32_t sf_bases[kMaxLayers];     // first float of layer l in a scale table
+};
+
+// Requester-side gather: every row whose owner has a direct source (the
+// owner's HBM mirror through NVLink, or this rank's own shard) is copied into
+// the output; padding rows become zero; FP8 scales are gathered for all rows.
+struct GatherParams {
+    const int32_t *indices;       // [layers][rows]
+    uint8_t *output;              // [layers][capacity][row_bytes]
+    float *sf_output;             // layer l at sf_output + l * sf_layer_stride
+    ErrorSink error;
+    LayerTable layer;
+    uint64_t direct_base[kMaxRanks];  // per owner; 0 = rows arrive by owner push
+    uint64_t sf_base[kMaxRanks];      // per scale shard
+    uint32_t layers, rows, tokens, ept;
+    uint32_t capacity, row_bytes, world, packs;
+    uint32_t sf_shard_div;        // global row -> shard: x / (n * sf_shard_div)
+    uint32_t sf_token_stride, sf_hidden_stride, sf_layer_stride;
+    uint32_t col_major_sf;
+    uint32_t sf_warps;            // warps per CTA dedicated to scales (0 for BF16)
+};
+
+// Requester-side dispatch for host-route owners: append (row, position) pairs
+// into each owner's inbox slot through peer stores, then the last CTA of each
+// layer publishes the per-owner mailbox headers.
+struct DispatchParams {
+    const int32_t *indices;
+    uint32_t *cursors;            // [layers][world] scratch, zero between fetches
+    uint32_t *layer_arrivals;     // [layers]
+    uint32_t *totals;             // [layers][world] rows requested this fetch
+    uint64_t *epochs;             // [layers][world] last published epoch
+    ErrorSink error;
+    LayerTable layer;
+    uint64_t inbox_base[kMaxRanks];   // owner arena inbox (peer mapping), 0 if direct
+    uint64_t header_base[kMaxRanks];  // owner host-shard header region (mapping)
+    uint32_t layers, rows, capacity, world, rank, channels;
+    uint32_t tile_rows;
+};
+
+struct PushTask {
+    uint32_t requester, layer, rows, first_block;
+    uint32_t rows_per_block, channels;
+    uint64_t epoch;
+};
+
+// Owner-side push: copy the requested rows from this rank's host shard (read
+// zero-copy) into each requester's output (peer stores), then release the
+// requester's done flag once every CTA of that task has finished.
+struct PushParams {
+    const uint8_t *table;         // this rank's host shard, mapped for this GPU
+    const uint64_t *inbox;        // this rank's inbox region [world][layers][capacity]
+    uint32_t *arrivals;           // [world][layers] scratch
+    ErrorSink error;
+    uint64_t out_base[kMaxRanks];     // requester arena output region (mapping)
+    uint64_t done_base[kMaxRanks];    // requester arena done region (mapping)
+    PushTask tasks[kMaxPushTasks];
+    uint32_t num_tasks, layers, world, rank, capacity, row_bytes;
+    uint64_t table_rows;
+};
+
+// Hook-side wait for one layer: every host-route owner that received a
+// non-empty request must publish the matching epoch in done[layer][owner].
+struct HookParams {
+    const uint32_t *totals;
+    const uint64_t *epochs;
+    const uint64_t *done;         // this rank's done region [layers][world]
+    ErrorSink error;
+    uint32_t layer, world;
+    uint64_t timeout_ns;
+};
+
+// Host launchers (defined in the .cu files).
+cudaError_t launch_gather(const GatherParams &p, int num_sms, cudaStream_t stream);
+cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream);
+cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream);
+cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream);
+// Bounded wait on a flag nothing sets; used by the timeout self-test.
+cudaError_t launch_wait_probe(const uint64_t *flag, uint64_t expected, uint64_t timeout_ns, ErrorSink error,
+                              cudaStream_t stream);
+
+} // namespace engram

@@ -1,0 +1,139 @@
+// Device primitives for the Engram data plane (sm_100a).
+//
+// Everything here is data movement and cross-GPU ordering; there is no math.
+// Ordering protocol used by every producer/consumer pair in this project:
+//   producer: data stores (local or peer) -> fence.sc.sys -> st.release.sys flag
+//   consumer: ld.acquire.sys flag (bounded poll) -> data loads
+// Waits are bounded by the global nanosecond timer and report through an error
+// record instead of trapping, so a missing peer never hangs or faults the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "params.h"
+
+namespace engram {
+
+struct alignas(16) Vec16 {
+    uint32_t x, y, z, w;
+};
+
+// 16-byte read-only load that bypasses L1 allocation; the table rows are read
+// once per fetch and must not evict the caller's working set from L1.
+__device__ __forceinline__ Vec16 ld_nc_na_v4(const void *ptr) {
+    Vec16 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+    return v;
+}
+
+// Plain 16-byte load for memory another agent may be writing concurrently
+// (host shards under a rewrite are quiesced by write(), so .nc is safe there
+// too; this variant is kept for the inbox, which peers fill).
+__device__ __forceinline__ Vec16 ld_v4(const void *ptr) {
+    Vec16 v;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(ptr));
+    return v;
+}
+
+__device__ __forceinline__ void st_v4(void *ptr, const Vec16 &v) {
+    asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Streaming store: the output is consumed by a later kernel, keep L1 clean.
+__device__ __forceinline__ void st_na_v4(void *ptr, const Vec16 &v) {
+    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const void *ptr) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u64(void *ptr, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u32(void *ptr, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Device-scope acq_rel fetch-add on a 32-bit counter (last-block-done pattern).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *ptr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(void *ptr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u32(void *ptr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// First reporter wins (device-scope CAS); it mirrors the record to the host
+// copy with the status written last.  Later reports only bump the count.
+__device__ __forceinline__ void report_error(const ErrorSink &sink, uint32_t code, uint32_t layer, uint32_t owner,
+                                             uint64_t observed, uint64_t expected) {
+    ErrorRecord *dev = sink.dev;
+    if (dev == nullptr)
+        return;
+    const uint32_t count = atomicAdd(&dev->count, 1u) + 1;
+    if (atomicCAS(&dev->status, 0u, code) != 0u) {
+        if (sink.host != nullptr)
+            st_relaxed_sys_u32(&sink.host->count, count);
+        return;
+    }
+    dev->layer = layer;
+    dev->owner = owner;
+    dev->observed = observed;
+    dev->expected = expected;
+    if (ErrorRecord *host = sink.host) {
+        st_relaxed_sys_u32(&host->layer, layer);
+        st_relaxed_sys_u32(&host->owner, owner);
+        st_relaxed_sys_u32(&host->count, count);
+        st_relaxed_sys_u64(&host->observed, observed);
+        st_relaxed_sys_u64(&host->expected, expected);
+        st_release_sys_u32(&host->status, code);
+    }
+}
+
+// Poll `flag` until it equals `expected` or `timeout_ns` passes.  Returns the
+// last value read.  Never traps; the caller reports a timeout.
+__device__ __forceinline__ uint64_t wait_flag_eq(const void *flag, uint64_t expected, uint64_t timeout_ns,
+                                                 bool *timed_out) {
+    const uint64_t start = global_timer_ns();
+    uint32_t backoff = 32;
+    uint64_t value = ld_acquire_sys_u64(flag);
+    while (value != expected) {
+        if (global_timer_ns() - start > timeout_ns) {
+            *timed_out = true;
+            return value;
+        }
+        __nanosleep(backoff);
+        backoff = backoff < 1024 ? backoff * 2 : 1024;
+        value = ld_acquire_sys_u64(flag);
+    }
+    *timed_out = false;
+    return value;
+}
+
+} // namespace engram

@@ -1,0 +1,871 @@
+// Native runtime of the B200 Engram buffer, exposed to Python as `_C.Runtime`.
+//
+// Parity: `engram_sge::Runtime` (sge_write/csrc/runtime.cpp:23-662) and the
+// native `deep_ep::engram::EngramBuffer` (deepep/csrc/buffers/engram.hpp).
+// Responsibilities:
+//   * allocate this rank's host shard and device arena (memory.h) and serve
+//     their descriptors to peers (fdpass.h);
+//   * map every same-node peer's shard and arena, probe the peer-HBM route per
+//     owner, and commit the negotiated route table into kernel parameters;
+//   * write(): fill the host shard, the optional HBM mirror and the FP8 scale
+//     table;
+//   * fetch(): enqueue dispatch (host-route owners) and gather (direct owners,
+//     padding, scales) on the caller's stream and return per-layer views;
+//   * wait_layer(): make the caller's stream depend on the fetch, enqueue the
+//     bounded done-flag wait for host-route owners, record the layer event;
+//   * run the owner service that launches push kernels for requesters.
+// Capture-aware event wiring follows the reference (runtime.cpp:412-568): an
+// eager fetch waits for the previous round's per-layer completion events;
+// under capture an internal event joins cross-stream hooks into the graph and
+// EXTERNAL events carry completion to work outside the graph.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "driver.h"
+#include "fdpass.h"
+#include "kernels/params.h"
+#include "memory.h"
+#include "owner_service.h"
+
+namespace py = pybind11;
+
+namespace engram {
+
+enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
+
+namespace {
+
+template <class T> T get(const py::dict &d, const char *key) {
+    if (!d.contains(key))
+        throw std::runtime_error(std::string("missing config key: ") + key);
+    return py::cast<T>(d[key]);
+}
+
+bool capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    check_cuda(cudaStreamIsCapturing(s, &st), "query capture status");
+    return st == cudaStreamCaptureStatusActive;
+}
+
+} // namespace
+
+class Runtime : public std::enable_shared_from_this<Runtime> {
+  public:
+    explicit Runtime(const py::dict &cfg) {
+        rank_ = get<uint32_t>(cfg, "rank");
+        world_ = get<uint32_t>(cfg, "world");
+        local_rank_ = get<uint32_t>(cfg, "local_rank");
+        local_size_ = get<uint32_t>(cfg, "local_size");
+        device_ = get<int>(cfg, "device");
+        entries_ = get<std::vector<uint32_t>>(cfg, "entries");
+        hidden_ = get<uint32_t>(cfg, "hidden");
+        elem_ = get<uint32_t>(cfg, "element_bytes");
+        max_tokens_ = get<uint32_t>(cfg, "max_tokens");
+        ept_ = get<uint32_t>(cfg, "ept");
+        packs_ = get<uint32_t>(cfg, "packs");
+        channels_ = get<uint32_t>(cfg, "channels");
+        egm_ = get<bool>(cfg, "egm");
+        local_sf_ = get<bool>(cfg, "local_sf");
+        timeout_ns_ = uint64_t(get<double>(cfg, "timeout_s") * 1e9);
+        token_ = get<std::string>(cfg, "token");
+        allow_host_vmm_ = get<bool>(cfg, "allow_host_vmm");
+        layers_ = uint32_t(entries_.size());
+        row_bytes_ = hidden_ * elem_;
+        capacity_ = max_tokens_ * ept_;
+        check(world_ >= 1 && world_ <= kMaxRanks, "world size out of range");
+        check(layers_ >= 1 && layers_ <= kMaxLayers, "layer count out of range");
+        check(rank_ < world_ && local_size_ >= 1 && world_ % local_size_ == 0 && local_rank_ == rank_ % local_size_,
+              "rank layout");
+        check(row_bytes_ % 16 == 0 && row_bytes_ > 0, "row bytes must be a positive multiple of 16");
+        check(channels_ >= 1 && channels_ <= 16, "channels out of range");
+        uint64_t at = 0, sf_at = 0;
+        for (uint32_t n : entries_) {
+            check(n > 0 && uint64_t(n) * world_ <= 0x7FFFFFFFull, "vocabulary index limit");
+            table_bases_.push_back(uint32_t(at));
+            sf_bases_.push_back(uint32_t(sf_at));
+            at += n;
+            sf_at += uint64_t(n) * (local_sf_ ? world_ : 1) * packs_;
+        }
+        check(at < (1ull << 32) && sf_at < (1ull << 32), "local vocabulary too large");
+        table_rows_ = at;
+
+        py::dict plan = get<py::dict>(cfg, "plan");
+        auto off = [&](const char *k) { return get<size_t>(plan, k); };
+        dev_mirror_ = off("dev_mirror");
+        dev_mirror_bytes_ = off("dev_mirror_bytes");
+        dev_sf_table_ = off("dev_sf_table");
+        dev_output_ = off("dev_output");
+        dev_sf_output_ = off("dev_sf_output");
+        dev_done_ = off("dev_done");
+        dev_inbox_ = off("dev_inbox");
+        dev_scratch_ = off("dev_scratch");
+        dev_scratch_bytes_ = off("dev_scratch_bytes");
+        device_bytes_ = off("device_bytes");
+        host_table_ = off("host_table");
+        host_headers_ = off("host_headers");
+        host_bytes_ = off("host_bytes");
+        check(!egm_ || dev_mirror_bytes_ == table_rows_ * row_bytes_, "mirror size does not match the vocabulary");
+
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaFree(nullptr), "initialise CUDA context");
+        check_cuda(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_), "SM count");
+        try {
+            arena_ = SharedAllocation::device(device_bytes_, device_);
+            host_ = SharedAllocation::host(host_bytes_, device_, allow_host_vmm_);
+            carve_scratch();
+            check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&host_error_), sizeof(ErrorRecord), cudaHostAllocMapped),
+                       "error record");
+            std::memset(host_error_, 0, sizeof(ErrorRecord));
+            check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&host_error_dev_), host_error_, 0),
+                       "error record device pointer");
+            check_cuda(cudaEventCreateWithFlags(&issued_, cudaEventDisableTiming), "issue event");
+            check_cuda(cudaEventCreateWithFlags(&capture_issued_, cudaEventDisableTiming), "capture event");
+            for (uint32_t l = 0; l < layers_; ++l) {
+                cudaEvent_t e;
+                check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "layer event");
+                finished_.push_back(e);
+            }
+            int lo = 0, hi = 0;
+            check_cuda(cudaDeviceGetStreamPriorityRange(&lo, &hi), "stream priorities");
+            check_cuda(cudaStreamCreateWithPriority(&owner_stream_, cudaStreamNonBlocking, hi), "owner stream");
+        } catch (...) {
+            release();
+            throw;
+        }
+        peer_host_.resize(world_);
+        peer_dev_.resize(world_);
+        routes_.assign(world_, kHostRoute);
+        mapping_errors_.assign(world_, "");
+    }
+
+    ~Runtime() { release(); }
+
+    // ------------------------------------------------------------- bootstrap
+    py::dict bootstrap() {
+        check(!closed_, "runtime closed");
+        if (!fd_server_)
+            fd_server_ = std::make_unique<FdServer>(socket_name(rank_), std::vector<int>{host_->fd(), arena_->fd()});
+        py::dict d;
+        d["pid"] = int(getpid());
+        d["socket"] = socket_name(rank_);
+        d["host_kind"] = int(host_->kind());
+        d["host_kind_name"] = memory_kind_name(host_->kind());
+        d["host_bytes"] = host_->bytes();
+        d["host_numa"] = host_->numa();
+        d["dev_bytes"] = arena_->bytes();
+        d["mirror"] = egm_;
+        d["mirror_offset"] = dev_mirror_;
+        d["mirror_bytes"] = egm_ ? dev_mirror_bytes_ : size_t(0);
+        d["config"] = py::make_tuple(world_, local_size_, entries_, hidden_, elem_, max_tokens_, ept_, packs_, egm_,
+                                     local_sf_, device_bytes_, host_bytes_);
+        return d;
+    }
+
+    py::dict probe_routes(const py::list &peers, const std::vector<int> &candidates) {
+        check(!probed_ && !closed_ && peers.size() == world_ && candidates.size() == world_, "route probe state");
+        routes_.assign(candidates.begin(), candidates.end());
+        mapping_errors_.assign(world_, "");
+        c10::cuda::CUDAGuard guard(device_);
+        for (uint32_t p = 0; p < world_; ++p) {
+            check(candidates[p] == kHostRoute || (candidates[p] == kPeerHbm && egm_), "invalid route candidate");
+            if (p == rank_)
+                continue;
+            py::dict d = peers[p].cast<py::dict>();
+            check(p / local_size_ == rank_ / local_size_,
+                  "owner " + std::to_string(p) + " is on another node; this transport spans one NVLink node");
+            // Mandatory mappings: every same-node peer's host shard (mailbox
+            // headers) and device arena (inbox, outputs, done flags).
+            const std::string sock = get<std::string>(d, "socket");
+            peer_host_[p] = std::make_unique<PeerMapping>(MemoryKind(get<int>(d, "host_kind")), fetch_fd(sock, 0),
+                                                          get<size_t>(d, "host_bytes"), device_,
+                                                          get<int>(d, "host_numa"));
+            peer_dev_[p] = std::make_unique<PeerMapping>(MemoryKind::DeviceVmm, fetch_fd(sock, 1),
+                                                         get<size_t>(d, "dev_bytes"), device_, -1);
+            check(peer_dev_[p]->bytes() >= device_bytes_ && peer_host_[p]->bytes() >= host_bytes_,
+                  "peer allocation smaller than the agreed plan");
+            if (candidates[p] != kPeerHbm)
+                continue;
+            try {
+                check(get<bool>(d, "mirror"), "owner keeps no HBM mirror");
+                check(get<size_t>(d, "mirror_bytes") == table_rows_ * row_bytes_ &&
+                          get<size_t>(d, "mirror_offset") == dev_mirror_,
+                      "owner HBM mirror size or offset mismatch");
+                check(peer_dev_[p]->readable(dev_mirror_, device_), "owner HBM mirror is not readable from this GPU");
+            } catch (const std::runtime_error &e) {
+                routes_[p] = kHostRoute;
+                mapping_errors_[p] = e.what();
+            }
+        }
+        routes_[rank_] = egm_ ? kPeerHbm : kHostRoute;
+        probed_ = true;
+        py::dict r;
+        r["routes"] = routes_;
+        r["errors"] = mapping_errors_;
+        return r;
+    }
+
+    void prepare_routes(const std::vector<int> &selected) {
+        check(probed_ && !ready_ && !closed_ && selected.size() == world_, "route commit state");
+        for (uint32_t p = 0; p < world_; ++p)
+            check(selected[p] <= routes_[p], "route exceeds probed capability");
+        routes_ = selected;
+        has_host_routes_ = false;
+        serves_any_ = false;
+        serve_.assign(world_, 0);
+        for (uint32_t p = 0; p < world_; ++p)
+            if (p != rank_ && routes_[p] == kHostRoute) {
+                has_host_routes_ = true;
+                serves_any_ = true;
+                serve_[p] = 1;
+            }
+        build_params();
+        // Every peer imported our descriptors during its probe, which finished
+        // before the probe reports were exchanged.
+        if (fd_server_) {
+            fds_served_ = fd_server_->served();
+            fd_server_.reset();
+        }
+        ready_ = true;
+    }
+
+    void connect() {
+        check(ready_ && !connected_ && !closed_, "connect state");
+        if (serves_any_) {
+            OwnerServiceConfig c;
+            c.world = world_;
+            c.layers = layers_;
+            c.capacity = capacity_;
+            c.rank = rank_;
+            c.headers = reinterpret_cast<const MailboxHeader *>(static_cast<uint8_t *>(host_->host_ptr()) +
+                                                                host_headers_);
+            c.serve = serve_;
+            const int dev = device_;
+            service_.start(
+                std::move(c), [this](const std::vector<PushTask> &batch) { launch_push_batch(batch); },
+                [dev] { check_cuda(cudaSetDevice(dev), "owner service device"); });
+        }
+        connected_ = true;
+    }
+
+    // ------------------------------------------------------------------ write
+    void write(uint32_t layer, const torch::Tensor &storage, const c10::optional<torch::Tensor> &scales) {
+        check_health();
+        check(ready_ && !closed_, "runtime not ready");
+        check(layer < layers_, "write layer out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        const size_t bytes = size_t(entries_[layer]) * row_bytes_;
+        check(size_t(storage.nbytes()) == bytes && storage.is_contiguous(), "storage shape");
+        uint8_t *dst = static_cast<uint8_t *>(host_->host_ptr()) + host_table_ + size_t(table_bases_[layer]) * row_bytes_;
+        if (storage.is_cuda())
+            check_cuda(cudaMemcpy(dst, storage.data_ptr(), bytes, cudaMemcpyDefault), "write vocabulary to host shard");
+        else
+            std::memcpy(dst, storage.data_ptr(), bytes);
+        if (egm_) {
+            void *mirror = reinterpret_cast<uint8_t *>(arena_->ptr()) + dev_mirror_ +
+                           size_t(table_bases_[layer]) * row_bytes_;
+            check_cuda(cudaMemcpy(mirror, dst, bytes, cudaMemcpyDefault), "write HBM mirror");
+        }
+        if (packs_) {
+            check(scales.has_value(), "missing scales");
+            const size_t rows = size_t(entries_[layer]) * (local_sf_ ? world_ : 1);
+            const size_t count = rows * packs_;
+            const auto &sf = *scales;
+            check(sf.scalar_type() == torch::kFloat32 && sf.is_contiguous() &&
+                      size_t(sf.numel()) == size_t(entries_[layer]) * world_ * packs_,
+                  "scale shape");
+            const float *src = sf.data_ptr<float>() + (local_sf_ ? 0 : size_t(rank_) * entries_[layer] * packs_);
+            void *target = reinterpret_cast<uint8_t *>(arena_->ptr()) + dev_sf_table_ + size_t(sf_bases_[layer]) * 4;
+            check_cuda(cudaMemcpy(target, src, count * 4, cudaMemcpyDefault), "write scale table");
+        }
+        check_cuda(cudaDeviceSynchronize(), "write synchronise");
+    }
+
+    // ------------------------------------------------------------------ fetch
+    py::list fetch(const torch::Tensor &indices, uint32_t channels, bool col_major) {
+        check_health();
+        check(connected_ && !closed_, "runtime is not connected");
+        check(indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_cuda() &&
+                  indices.is_contiguous() && indices.size(0) == layers_ && indices.size(2) == ept_ &&
+                  indices.size(1) <= max_tokens_ && indices.get_device() == device_,
+              "indices must be contiguous CUDA int32 [layers, tokens, ept]");
+        check(channels >= 1 && channels <= channels_, "channels exceed the allocation");
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        issue_captured_ = capturing(s);
+        issue_stream_ = s;
+        if (!issue_captured_)
+            for (auto e : finished_)
+                check_cuda(cudaStreamWaitEvent(s, e, 0), "workspace reuse dependency");
+        tokens_ = uint32_t(indices.size(1));
+        const uint32_t rows = tokens_ * ept_;
+        uint32_t ts, hs, ls;
+        sf_strides(tokens_, col_major, &ts, &hs, &ls);
+        const int32_t *idx = indices.data_ptr<int32_t>();
+        if (rows > 0) {
+            if (has_host_routes_) {
+                DispatchParams d = dispatch_;
+                d.indices = idx;
+                d.rows = rows;
+                d.channels = channels;
+                check_cuda(launch_dispatch(d, s), "launch dispatch");
+                ++launches_;
+            }
+            GatherParams g = gather_;
+            g.indices = idx;
+            g.rows = rows;
+            g.tokens = tokens_;
+            g.sf_token_stride = ts;
+            g.sf_hidden_stride = hs;
+            g.sf_layer_stride = ls;
+            g.col_major_sf = col_major ? 1 : 0;
+            check_cuda(launch_gather(g, num_sms_, s), "launch gather");
+            ++launches_;
+        }
+        if (issue_captured_) {
+            check_cuda(cudaEventRecord(capture_issued_, s), "record capture issue");
+            check_cuda(cudaEventRecordWithFlags(issued_, s, cudaEventRecordExternal), "record external issue");
+        } else {
+            check_cuda(cudaEventRecord(issued_, s), "record issue");
+        }
+        ++fetches_;
+        return make_outputs(ts, hs, ls);
+    }
+
+    void wait_layer(uint32_t layer) {
+        check_health();
+        check(connected_ && !closed_, "runtime is not connected");
+        check(layer < layers_, "hook layer out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        bool source_active = issue_captured_ && capturing(issue_stream_);
+        if (source_active) {
+            check_cuda(cudaStreamWaitEvent(s, capture_issued_, 0), "capture issue to hook dependency");
+        } else {
+            check_cuda(cudaStreamWaitEvent(s, issued_, capturing(s) ? cudaEventWaitExternal : 0),
+                       "issue to hook dependency");
+        }
+        if (has_host_routes_ && tokens_ > 0) {
+            HookParams h{};
+            h.totals = totals_;
+            h.epochs = epochs_;
+            h.done = reinterpret_cast<const uint64_t *>(arena_->ptr() + dev_done_);
+            h.error = sink();
+            h.layer = layer;
+            h.world = world_;
+            h.timeout_ns = timeout_ns_;
+            check_cuda(launch_hook_wait(h, s), "launch hook wait");
+            ++launches_;
+        }
+        check_cuda(cudaEventRecordWithFlags(finished_[layer], s, capturing(s) ? cudaEventRecordExternal : 0),
+                   "record layer completion");
+    }
+
+    // ------------------------------------------------------------- inspection
+    void check_health() {
+        service_.check();
+        if (host_error_ != nullptr) {
+            volatile ErrorRecord *e = host_error_;
+            if (e->status != 0)
+                throw std::runtime_error(describe_error());
+        }
+    }
+
+    py::dict error_state() {
+        py::dict d;
+        volatile ErrorRecord *e = host_error_;
+        d["status"] = e ? e->status : 0u;
+        d["layer"] = e ? e->layer : 0u;
+        d["owner"] = e ? e->owner : 0u;
+        d["count"] = e ? e->count : 0u;
+        d["observed"] = e ? e->observed : 0ull;
+        d["expected"] = e ? e->expected : 0ull;
+        d["owner_service_error"] = service_.error();
+        return d;
+    }
+
+    py::dict memory_usage() {
+        py::dict d;
+        d["rank"] = rank_;
+        d["device_allocation_bytes"] = arena_ ? arena_->bytes() : 0;
+        d["host_allocation_bytes"] = host_ ? host_->bytes() : 0;
+        d["output_bytes"] = size_t(layers_) * capacity_ * row_bytes_;
+        d["cpu_vocabulary_bytes"] = size_t(table_rows_) * row_bytes_;
+        d["hbm_mirror_bytes"] = egm_ ? dev_mirror_bytes_ : size_t(0);
+        d["mailbox_bytes"] = size_t(world_) * layers_ * kHeaderBytes;
+        d["inbox_bytes"] = size_t(world_) * layers_ * capacity_ * 8;
+        d["owner_threads"] = service_.running() ? 1 : 0;
+        d["served_requests"] = service_.requests();
+        d["served_rows"] = service_.rows();
+        d["push_batches"] = service_.batches();
+        d["egm_enabled"] = egm_;
+        bool direct_remote = false;
+        for (uint32_t p = 0; p < world_; ++p)
+            direct_remote |= (p != rank_ && routes_[p] == kPeerHbm);
+        d["has_egm_routes"] = direct_remote;
+        d["has_host_routes"] = has_host_routes_;
+        d["routes"] = routes_;
+        d["egm_mapping_errors"] = mapping_errors_;
+        d["local_sf"] = local_sf_;
+        d["table_numa"] = host_ ? host_->numa() : -1;
+        d["host_memory_kind"] = host_ ? memory_kind_name(host_->kind()) : "none";
+        d["host_memory_note"] = host_ ? host_->note() : "";
+        d["cpu_vocabulary_allocations"] = 1;
+        d["cpu_vocabulary_allocated_bytes"] = host_ ? host_->bytes() : 0;
+        d["fd_transport"] = "unix_socket_scm_rights";
+        d["fds_served"] = fds_served_;
+        d["fetches"] = fetches_;
+        d["kernel_launches"] = launches_;
+        d["num_sms"] = num_sms_;
+        return d;
+    }
+
+    // Synchronous snapshot of the per-(layer, owner) counters (tests only).
+    py::dict debug_state() {
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaDeviceSynchronize(), "debug sync");
+        const size_t n = size_t(layers_) * world_;
+        std::vector<uint64_t> epochs(n), done(n);
+        std::vector<uint32_t> totals(n);
+        check_cuda(cudaMemcpy(epochs.data(), epochs_, n * 8, cudaMemcpyDeviceToHost), "read epochs");
+        check_cuda(cudaMemcpy(totals.data(), totals_, n * 4, cudaMemcpyDeviceToHost), "read totals");
+        check_cuda(cudaMemcpy(done.data(), reinterpret_cast<void *>(arena_->ptr() + dev_done_), n * 8,
+                              cudaMemcpyDeviceToHost),
+                   "read done flags");
+        std::vector<uint64_t> served;
+        for (uint32_t r = 0; r < world_; ++r)
+            for (uint32_t l = 0; l < layers_; ++l)
+                served.push_back(service_.completed(r, l));
+        py::dict d;
+        d["epochs"] = epochs;
+        d["totals"] = totals;
+        d["done"] = done;
+        d["served_epochs"] = served;
+        return d;
+    }
+
+    // Bounded wait on a flag nothing sets: the GPU must give up after
+    // `timeout_ms` and report a timeout without faulting (tests only).
+    py::dict run_wait_probe(double timeout_ms) {
+        c10::cuda::CUDAGuard guard(device_);
+        uint64_t *flag = nullptr;
+        ErrorRecord *dev = nullptr, *host = nullptr, *host_dev = nullptr;
+        check_cuda(cudaMalloc(&flag, 8), "probe flag");
+        check_cuda(cudaMalloc(&dev, sizeof(ErrorRecord)), "probe record");
+        check_cuda(cudaMemset(flag, 0, 8), "clear probe flag");
+        check_cuda(cudaMemset(dev, 0, sizeof(ErrorRecord)), "clear probe record");
+        check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&host), sizeof(ErrorRecord), cudaHostAllocMapped),
+                   "probe host record");
+        std::memset(host, 0, sizeof(ErrorRecord));
+        check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&host_dev), host, 0), "probe host pointer");
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, s);
+        check_cuda(launch_wait_probe(flag, 1, uint64_t(timeout_ms * 1e6), ErrorSink{dev, host_dev}, s), "probe");
+        cudaEventRecord(b, s);
+        check_cuda(cudaStreamSynchronize(s), "probe synchronise");
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        py::dict d;
+        volatile ErrorRecord *h = host;
+        d["status"] = h->status;
+        d["observed"] = h->observed;
+        d["expected"] = h->expected;
+        d["elapsed_ms"] = ms;
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        cudaFree(flag);
+        cudaFree(dev);
+        cudaFreeHost(host);
+        return d;
+    }
+
+    void close() {
+        if (closed_)
+            return;
+        {
+            c10::cuda::CUDAGuard guard(device_);
+            cudaError_t rc = cudaDeviceSynchronize();
+            py::gil_scoped_release release;
+            service_.stop_and_join();
+            if (owner_stream_)
+                cudaStreamSynchronize(owner_stream_);
+            check_cuda(rc, "synchronise before close");
+        }
+        fd_server_.reset();
+        peer_dev_.clear();
+        peer_host_.clear();
+        closed_ = true;
+        connected_ = false;
+    }
+
+    bool closed() const { return closed_; }
+
+  private:
+    std::string socket_name(uint32_t r) const { return "engram-b200." + token_ + "." + std::to_string(r); }
+
+    ErrorSink sink() const { return ErrorSink{dev_error_, host_error_dev_}; }
+
+    void carve_scratch() {
+        uint8_t *base = reinterpret_cast<uint8_t *>(arena_->ptr()) + dev_scratch_;
+        size_t at = 0;
+        auto take = [&](size_t bytes) {
+            at = align_up(at, 16);
+            uint8_t *p = base + at;
+            at += bytes;
+            return p;
+        };
+        const size_t lw = size_t(layers_) * world_;
+        epochs_ = reinterpret_cast<uint64_t *>(take(lw * 8));
+        totals_ = reinterpret_cast<uint32_t *>(take(lw * 4));
+        cursors_ = reinterpret_cast<uint32_t *>(take(lw * 4));
+        layer_arrivals_ = reinterpret_cast<uint32_t *>(take(layers_ * 4));
+        push_arrivals_ = reinterpret_cast<uint32_t *>(take(lw * 4));
+        dev_error_ = reinterpret_cast<ErrorRecord *>(take(sizeof(ErrorRecord)));
+        check(at <= dev_scratch_bytes_, "scratch region too small");
+    }
+
+    void sf_strides(uint32_t tokens, bool col_major, uint32_t *ts, uint32_t *hs, uint32_t *ls) const {
+        if (col_major) {
+            *ts = 1;
+            *hs = (tokens + 3) / 4 * 4;
+            *ls = *hs * ept_ * packs_;
+        } else {
+            *ts = ept_ * packs_;
+            *hs = 1;
+            *ls = tokens * ept_ * packs_;
+        }
+    }
+
+    void build_params() {
+        LayerTable lt{};
+        for (uint32_t l = 0; l < layers_; ++l) {
+            lt.entries[l] = entries_[l];
+            lt.table_bases[l] = table_bases_[l];
+            lt.sf_bases[l] = sf_bases_[l];
+        }
+        const uint64_t arena = arena_->ptr();
+        GatherParams &g = gather_;
+        g = GatherParams{};
+        g.output = reinterpret_cast<uint8_t *>(arena + dev_output_);
+        g.sf_output = reinterpret_cast<float *>(arena + dev_sf_output_);
+        g.error = sink();
+        g.layer = lt;
+        for (uint32_t o = 0; o < world_; ++o) {
+            if (o == rank_)
+                g.direct_base[o] = egm_ ? arena + dev_mirror_ : host_->ptr() + host_table_;
+            else if (routes_[o] == kPeerHbm)
+                g.direct_base[o] = peer_dev_[o]->ptr() + dev_mirror_;
+            else
+                g.direct_base[o] = 0;
+        }
+        if (local_sf_) {
+            g.sf_base[0] = arena + dev_sf_table_;
+            g.sf_shard_div = world_;
+        } else {
+            for (uint32_t o = 0; o < world_; ++o)
+                g.sf_base[o] = o == rank_ ? arena + dev_sf_table_ : peer_dev_[o]->ptr() + dev_sf_table_;
+            g.sf_shard_div = 1;
+        }
+        g.layers = layers_;
+        g.ept = ept_;
+        g.capacity = capacity_;
+        g.row_bytes = row_bytes_;
+        g.world = world_;
+        g.packs = packs_;
+        g.sf_warps = packs_ ? 2 : 0;
+
+        DispatchParams &d = dispatch_;
+        d = DispatchParams{};
+        d.cursors = cursors_;
+        d.layer_arrivals = layer_arrivals_;
+        d.totals = totals_;
+        d.epochs = epochs_;
+        d.error = sink();
+        d.layer = lt;
+        for (uint32_t o = 0; o < world_; ++o) {
+            const bool host = o != rank_ && routes_[o] == kHostRoute;
+            d.inbox_base[o] = host ? peer_dev_[o]->ptr() + dev_inbox_ : 0;
+            d.header_base[o] = host ? peer_host_[o]->ptr() + host_headers_ : 0;
+        }
+        d.layers = layers_;
+        d.capacity = capacity_;
+        d.world = world_;
+        d.rank = rank_;
+        d.tile_rows = 4096;
+
+        PushParams &p = push_template_;
+        p = PushParams{};
+        p.table = reinterpret_cast<const uint8_t *>(host_->ptr() + host_table_);
+        p.inbox = reinterpret_cast<const uint64_t *>(arena + dev_inbox_);
+        p.arrivals = push_arrivals_;
+        p.error = sink();
+        for (uint32_t r = 0; r < world_; ++r) {
+            const bool serve = r != rank_ && routes_[r] == kHostRoute;
+            p.out_base[r] = serve ? peer_dev_[r]->ptr() + dev_output_ : 0;
+            p.done_base[r] = serve ? peer_dev_[r]->ptr() + dev_done_ : 0;
+        }
+        p.layers = layers_;
+        p.world = world_;
+        p.rank = rank_;
+        p.capacity = capacity_;
+        p.row_bytes = row_bytes_;
+        p.table_rows = table_rows_;
+    }
+
+    // Runs on the owner-service thread.
+    void launch_push_batch(const std::vector<PushTask> &batch) {
+        size_t at = 0;
+        while (at < batch.size()) {
+            PushParams p = push_template_;
+            const size_t n = std::min(batch.size() - at, size_t(kMaxPushTasks));
+            uint32_t blocks = 0;
+            for (size_t i = 0; i < n; ++i) {
+                PushTask t = batch[at + i];
+                const uint32_t ch = std::max(1u, std::min(t.channels, 16u));
+                const uint32_t max_blocks = ch * 16;
+                uint32_t want = (t.rows + 63) / 64;
+                want = std::max(1u, std::min(want, max_blocks));
+                uint32_t rpb = (t.rows + want - 1) / want;
+                rpb = (rpb + 63) / 64 * 64;
+                t.rows_per_block = rpb;
+                t.first_block = blocks;
+                blocks += (t.rows + rpb - 1) / rpb;
+                p.tasks[i] = t;
+            }
+            p.num_tasks = uint32_t(n);
+            check_cuda(launch_push(p, int(blocks), owner_stream_), "launch push");
+            at += n;
+        }
+    }
+
+    py::list make_outputs(uint32_t ts, uint32_t hs, uint32_t sf_layer_stride) {
+        py::list out;
+        auto keep = shared_from_this();
+        const auto dtype = packs_ ? torch::kFloat8_e4m3fn : torch::kBFloat16;
+        auto opts = torch::TensorOptions().dtype(dtype).device(torch::Device(torch::kCUDA, device_));
+        auto fopts = torch::TensorOptions().dtype(torch::kFloat32).device(torch::Device(torch::kCUDA, device_));
+        const uint64_t arena = arena_->ptr();
+        for (uint32_t l = 0; l < layers_; ++l) {
+            void *ptr = reinterpret_cast<void *>(arena + dev_output_ + uint64_t(l) * capacity_ * row_bytes_);
+            auto data = torch::from_blob(ptr, {int64_t(tokens_), int64_t(hidden_) * ept_}, [keep](void *) {}, opts);
+            if (packs_) {
+                void *sptr = reinterpret_cast<void *>(arena + dev_sf_output_ + uint64_t(l) * sf_layer_stride * 4);
+                auto scales = torch::from_blob(sptr, {int64_t(tokens_), int64_t(ept_) * packs_},
+                                               {int64_t(ts), int64_t(hs)}, [keep](void *) {}, fopts);
+                out.append(py::make_tuple(data, scales));
+            } else {
+                out.append(data);
+            }
+        }
+        return out;
+    }
+
+    void release() noexcept {
+        service_.stop_and_join();
+        fd_server_.reset();
+        peer_dev_.clear();
+        peer_host_.clear();
+        if (issued_)
+            cudaEventDestroy(issued_);
+        if (capture_issued_)
+            cudaEventDestroy(capture_issued_);
+        for (auto e : finished_)
+            cudaEventDestroy(e);
+        finished_.clear();
+        issued_ = capture_issued_ = nullptr;
+        if (owner_stream_) {
+            cudaStreamSynchronize(owner_stream_);
+            cudaStreamDestroy(owner_stream_);
+            owner_stream_ = nullptr;
+        }
+        if (host_error_) {
+            cudaFreeHost(host_error_);
+            host_error_ = nullptr;
+        }
+        host_.reset();
+        arena_.reset();
+    }
+
+    // configuration
+    uint32_t rank_ = 0, world_ = 1, local_rank_ = 0, local_size_ = 1, layers_ = 0;
+    int device_ = 0, num_sms_ = 0;
+    std::vector<uint32_t> entries_, table_bases_, sf_bases_;
+    uint32_t hidden_ = 0, elem_ = 0, max_tokens_ = 0, ept_ = 0, packs_ = 0, channels_ = 1;
+    uint32_t row_bytes_ = 0, capacity_ = 0;
+    uint64_t table_rows_ = 0, timeout_ns_ = 0;
+    bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
+    std::string token_;
+    size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
+           dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;
+    size_t host_table_ = 0, host_headers_ = 0, host_bytes_ = 0;
+    // memory
+    std::unique_ptr<SharedAllocation> arena_, host_;
+    std::vector<std::unique_ptr<PeerMapping>> peer_host_, peer_dev_;
+    std::unique_ptr<FdServer> fd_server_;
+    long fds_served_ = 0;
+    uint64_t *epochs_ = nullptr;
+    uint32_t *totals_ = nullptr, *cursors_ = nullptr, *layer_arrivals_ = nullptr, *push_arrivals_ = nullptr;
+    ErrorRecord *dev_error_ = nullptr, *host_error_ = nullptr, *host_error_dev_ = nullptr;
+    // routes
+    std::vector<int> routes_;
+    std::vector<std::string> mapping_errors_;
+    std::vector<uint8_t> serve_;
+    bool probed_ = false, ready_ = false, connected_ = false, closed_ = false;
+    bool has_host_routes_ = false, serves_any_ = false;
+    GatherParams gather_{};
+    DispatchParams dispatch_{};
+    PushParams push_template_{};
+    // streams and events
+    cudaEvent_t issued_ = nullptr, capture_issued_ = nullptr;
+    std::vector<cudaEvent_t> finished_;
+    cudaStream_t issue_stream_ = nullptr, owner_stream_ = nullptr;
+    bool issue_captured_ = false;
+    uint32_t tokens_ = 0;
+    uint64_t fetches_ = 0, launches_ = 0;
+    OwnerService service_;
+
+    std::string describe_error() const {
+        volatile ErrorRecord *e = host_error_;
+        static const char *names[] = {"ok", "hook wait timed out", "index outside the vocabulary",
+                                      "inbox overflow", "push bounds"};
+        const uint32_t s = e->status;
+        std::string what = s < 5 ? names[s] : "unknown error";
+        return "Engram device error: " + what + " (layer " + std::to_string(e->layer) + ", owner " +
+               std::to_string(e->owner) + ", observed " + std::to_string(e->observed) + ", expected " +
+               std::to_string(e->expected) + ", reports " + std::to_string(e->count) + ")";
+    }
+};
+
+// -------------------------------------------------------------------------
+// CPU test harnesses: the owner service and descriptor passing without a GPU.
+
+class OwnerServiceHarness {
+  public:
+    OwnerServiceHarness(uint32_t world, uint32_t layers, uint32_t capacity, std::vector<uint8_t> serve)
+        : world_(world), layers_(layers), capacity_(capacity), serve_(std::move(serve)),
+          headers_(size_t(world) * layers) {
+        std::memset(headers_.data(), 0, headers_.size() * sizeof(MailboxHeader));
+    }
+    ~OwnerServiceHarness() { service_.stop_and_join(); }
+
+    void publish(uint32_t requester, uint32_t layer, uint64_t epoch, uint32_t rows, uint32_t channels) {
+        MailboxHeader *h = &headers_.at(size_t(requester) * layers_ + layer);
+        __atomic_store_n(&h->rows, rows, __ATOMIC_RELAXED);
+        __atomic_store_n(&h->layer, layer, __ATOMIC_RELAXED);
+        __atomic_store_n(&h->requester, requester, __ATOMIC_RELAXED);
+        __atomic_store_n(&h->channels, channels, __ATOMIC_RELAXED);
+        __atomic_store_n(&h->ready, epoch, __ATOMIC_RELEASE);
+    }
+    void start(int fail_after) {
+        OwnerServiceConfig c;
+        c.world = world_;
+        c.layers = layers_;
+        c.capacity = capacity_;
+        c.headers = headers_.data();
+        c.serve = serve_;
+        c.idle_spin_us = 1000;
+        c.nap_us = 20;
+        fail_after_ = fail_after;
+        service_.start(std::move(c), [this](const std::vector<PushTask> &batch) {
+            std::lock_guard<std::mutex> lock(mu_);
+            for (const auto &t : batch) {
+                if (fail_after_ >= 0 && int(launched_.size()) >= fail_after_)
+                    throw std::runtime_error("injected launch failure");
+                launched_.push_back(t);
+            }
+        });
+    }
+    void stop() {
+        py::gil_scoped_release release;
+        service_.stop_and_join();
+    }
+    py::list launched() {
+        std::lock_guard<std::mutex> lock(mu_);
+        py::list out;
+        for (const auto &t : launched_)
+            out.append(py::make_tuple(t.requester, t.layer, t.rows, t.epoch, t.channels));
+        return out;
+    }
+    std::string error() { return service_.error(); }
+    void check() { service_.check(); }
+    bool running() const { return service_.running(); }
+
+  private:
+    uint32_t world_, layers_, capacity_;
+    std::vector<uint8_t> serve_;
+    std::vector<MailboxHeader> headers_;
+    OwnerService service_;
+    std::mutex mu_;
+    std::vector<PushTask> launched_;
+    int fail_after_ = -1;
+};
+
+int memfd_with_bytes(const std::string &data) {
+    int fd = memfd_create("engram-test", MFD_CLOEXEC);
+    check(fd >= 0, "memfd_create");
+    check(ftruncate(fd, off_t(data.size())) == 0, "ftruncate");
+    check(pwrite(fd, data.data(), data.size(), 0) == ssize_t(data.size()), "pwrite");
+    return fd;
+}
+
+py::bytes read_fd_bytes(int fd, size_t n) {
+    std::string out(n, '\0');
+    check(pread(fd, out.data(), n, 0) == ssize_t(n), "pread");
+    return py::bytes(out);
+}
+
+} // namespace engram
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    using namespace engram;
+    m.doc() = "B200 Engram runtime: VMM shards, peer mappings, sm_100a gather/dispatch/push kernels";
+    m.attr("MAX_RANKS") = kMaxRanks;
+    m.attr("MAX_LAYERS") = kMaxLayers;
+    m.attr("HEADER_BYTES") = kHeaderBytes;
+    m.attr("MAX_PUSH_TASKS") = kMaxPushTasks;
+    m.attr("KERNELS") = py::make_tuple("gather_kernel", "dispatch_kernel", "push_kernel", "hook_wait_kernel");
+    py::class_<Runtime, std::shared_ptr<Runtime>>(m, "Runtime")
+        .def(py::init<const py::dict &>())
+        .def("bootstrap", &Runtime::bootstrap)
+        .def("probe_routes", &Runtime::probe_routes)
+        .def("prepare_routes", &Runtime::prepare_routes)
+        .def("connect", &Runtime::connect)
+        .def("write", &Runtime::write, py::arg("layer"), py::arg("storage"), py::arg("scales") = py::none())
+        .def("fetch", &Runtime::fetch)
+        .def("wait_layer", &Runtime::wait_layer)
+        .def("check_health", &Runtime::check_health)
+        .def("error_state", &Runtime::error_state)
+        .def("memory_usage", &Runtime::memory_usage)
+        .def("debug_state", &Runtime::debug_state)
+        .def("run_wait_probe", &Runtime::run_wait_probe)
+        .def("close", &Runtime::close)
+        .def_property_readonly("closed", &Runtime::closed);
+    py::class_<OwnerServiceHarness>(m, "OwnerServiceHarness")
+        .def(py::init<uint32_t, uint32_t, uint32_t, std::vector<uint8_t>>())
+        .def("publish", &OwnerServiceHarness::publish)
+        .def("start", &OwnerServiceHarness::start, py::arg("fail_after") = -1)
+        .def("stop", &OwnerServiceHarness::stop)
+        .def("launched", &OwnerServiceHarness::launched)
+        .def("error", &OwnerServiceHarness::error)
+        .def("check", &OwnerServiceHarness::check)
+        .def_property_readonly("running", &OwnerServiceHarness::running);
+    py::class_<FdServer>(m, "FdServer")
+        .def(py::init<const std::string &, std::vector<int>>())
+        .def("stop", &FdServer::stop)
+        .def_property_readonly("served", &FdServer::served);
+    m.def("fetch_fd", &fetch_fd, py::arg("name"), py::arg("index"), py::arg("timeout_s") = 30.0);
+    m.def("memfd_with_bytes", &memfd_with_bytes);
+    m.def("read_fd_bytes", &read_fd_bytes);
+}

@@ -1,0 +1,172 @@
+"""Lifecycle and argument checks shared by every EngramBuffer implementation.
+
+The public contract (reference ``sge_write/engram_sge_write/buffer.py:39-352``
+and ``deepep/deep_ep/buffers/engram.py:42-297``):
+
+* construction, ``set_config``, ``write`` and ``destroy`` are collective over the
+  group;
+* ``fetch(indices)`` submits every layer's lookup on the current CUDA stream and
+  returns one hook per layer; a hook submits that layer's wait on the stream
+  current at hook time and returns the layer's output view (``data`` for BF16,
+  ``(data, scales)`` for FP8);
+* one fetch is outstanding at a time: a second ``fetch`` before every hook was
+  called raises, and a hook of a superseded fetch raises;
+* ``destroy`` requires ``explicitly_destroy=True`` and no outstanding hooks.
+"""
+
+from __future__ import annotations
+
+import functools
+import warnings
+from abc import ABC, abstractmethod
+
+import torch
+import torch.distributed as dist
+
+from .layout import EngramConfig, validate_config
+
+
+def accept_legacy_storage_size(init):
+    """Accept the reference's older ``num_rdma_storage_size`` keyword."""
+
+    @functools.wraps(init)
+    def wrapped(self, *args, **kwargs):
+        if "num_rdma_storage_size" in kwargs:
+            if "num_rdma_storage_bytes" in kwargs:
+                raise TypeError("Specify only one of num_rdma_storage_bytes and num_rdma_storage_size")
+            kwargs["num_rdma_storage_bytes"] = kwargs.pop("num_rdma_storage_size")
+        return init(self, *args, **kwargs)
+
+    return wrapped
+
+
+class EngramBufferBase(ABC):
+    """Host-side state machine common to the native and the torch buffers."""
+
+    impl_name = "base"
+
+    def __init__(self, group, explicitly_destroy: bool):
+        self.group = group
+        self.rank_idx = group.rank()
+        self.num_ranks = group.size()
+        self.explicitly_destroy = explicitly_destroy
+        self._config: EngramConfig | None = None
+        self._configured = False
+        self._written = False
+        self._generation = 0
+        self._pending: set = set()
+        self._input = None
+        self._destroyed = False
+
+    # ------------------------------------------------------------------ checks
+    def _ready(self):
+        if self._destroyed or not self._configured:
+            raise RuntimeError("Buffer is unconfigured or destroyed")
+
+    def _check_config_args(self, entries, hidden, max_tokens, ept, dtype, num_sf_packs) -> EngramConfig:
+        if self._configured:
+            raise RuntimeError("set_config is initialization-only; create a new Buffer to reconfigure")
+        return validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, self.num_ranks)
+
+    def _check_write_args(self, storages, sfs, device_index):
+        self._ready()
+        if self._pending:
+            raise RuntimeError("Call all outstanding hooks before replacing vocabulary contents")
+        c = self._config
+        if len(storages) != c.layers or (c.num_sf_packs and (sfs is None or len(sfs) != c.layers)):
+            raise ValueError("One storage/scales tensor is required per layer")
+        for layer, (storage, n) in enumerate(zip(storages, c.entries)):
+            if tuple(storage.shape) != (n, c.hidden) or storage.dtype != c.dtype or not storage.is_contiguous():
+                raise ValueError(f"Invalid vocabulary tensor for layer {layer}")
+            if storage.is_cuda and device_index is not None and storage.device.index != device_index:
+                raise ValueError("Vocabulary CUDA tensor is on the wrong device")
+            if c.num_sf_packs:
+                sf = sfs[layer]
+                if (
+                    tuple(sf.shape) != (self.num_ranks * n, c.num_sf_packs)
+                    or sf.dtype != torch.float32
+                    or not sf.is_contiguous()
+                ):
+                    raise ValueError(f"Invalid global scale tensor for layer {layer}")
+                if sf.is_cuda and device_index is not None and sf.device.index != device_index:
+                    raise ValueError("Scale CUDA tensor is on the wrong device")
+
+    def _check_fetch_args(self, indices, device_index, require_cuda: bool):
+        self._ready()
+        if not self._written:
+            raise RuntimeError("write() must initialize the vocabulary before fetch()")
+        if self._pending:
+            raise RuntimeError("Call every previous layer hook before the next fetch")
+        c = self._config
+        ok = (
+            isinstance(indices, torch.Tensor)
+            and indices.ndim == 3
+            and indices.shape[0] == c.layers
+            and indices.shape[2] == c.ept
+            and 0 <= indices.shape[1] <= c.max_tokens
+            and indices.dtype == torch.int32
+            and indices.is_contiguous()
+        )
+        if ok and require_cuda:
+            ok = indices.is_cuda and (device_index is None or indices.device.index == device_index)
+        if not ok:
+            where = "CUDA " if require_cuda else ""
+            raise ValueError(
+                f"indices must be contiguous {where}int32 [layers, tokens, entries_per_token] within capacity"
+            )
+
+    def _make_hooks(self, generation, wait_layer, outputs):
+        def make(layer):
+            def hook():
+                self._ready()
+                if generation != self._generation:
+                    raise RuntimeError("This hook belongs to a superseded fetch")
+                if layer not in self._pending:
+                    raise RuntimeError("This layer hook was already called")
+                wait_layer(layer)
+                self._pending.discard(layer)
+                return outputs[layer]
+
+            return hook
+
+        return [make(layer) for layer in range(self._config.layers)]
+
+    def _begin_fetch(self):
+        self._generation += 1
+        self._pending = set(range(self._config.layers))
+        return self._generation
+
+    # ---------------------------------------------------------------- shared API
+    def barrier(self):
+        """Host barrier over the group (not a stream operation; never capture it)."""
+        if torch.cuda.is_available() and torch.cuda.is_initialized():
+            torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def get_comm_stream(self):
+        """The stream fetch/hooks submit to: the caller's current stream."""
+        if torch.cuda.is_available():
+            return torch.cuda.current_stream()
+        return None
+
+    @property
+    def main_context(self):
+        return getattr(self, "runtime", None)
+
+    @abstractmethod
+    def destroy(self):  # pragma: no cover - interface
+        ...
+
+    def _check_destroy(self):
+        if not self.explicitly_destroy:
+            raise RuntimeError("Set explicitly_destroy=True before calling destroy()")
+        if self._pending and not self._destroyed:
+            raise RuntimeError("Outstanding layer hooks must be called before destroy()")
+
+    def __del__(self):
+        if getattr(self, "explicitly_destroy", False) and not getattr(self, "_destroyed", True) and getattr(
+            self, "_configured", False
+        ):
+            warnings.warn(
+                f"{type(self).__name__} was not collectively destroyed before process shutdown", ResourceWarning
+            )

@@ -1,0 +1,199 @@
+"""Per-rank memory plan shared by the native runtime and the torch oracle.
+
+Every rank owns two exportable allocations:
+
+* a **host shard** (pinned host memory, CUDA-VMM ``HOST_NUMA`` when the driver
+  supports it): the vocabulary rows of every layer back to back, followed by the
+  mailbox headers that requesters' GPUs write and this rank's owner service
+  polls;
+* a **device arena** (one CUDA-VMM ``DEVICE`` allocation): the optional HBM
+  mirror of the vocabulary, the FP8 scale table, the per-layer output region,
+  the scale output, the per-(layer, owner) done flags, the request inbox that
+  requesters fill, and small scratch words.
+
+Row ``x`` of layer ``l`` is owned by rank ``x // n_l`` and stored there as local
+row ``x % n_l`` at ``table_bases[l] + x % n_l`` (reference:
+``sge_write/csrc/gpu_request.cu:20,103,187-188``, ``runtime.cpp:137-148``).
+Output rows of layer ``l`` live at ``output + (l * capacity + at) * row_bytes``
+with ``capacity = max_tokens * ept`` (reference ``runtime.cpp:151-156, 519-522``).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+REGION_ALIGN = 4096
+ALLOC_ALIGN = 2 << 20
+HEADER_BYTES = 64
+MAX_RANKS = 64
+MAX_LAYERS = 32
+
+
+def align(n: int, a: int) -> int:
+    return (n + a - 1) // a * a
+
+
+def ceil_div(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+@dataclass(frozen=True)
+class EngramConfig:
+    entries: tuple  # per-rank rows per layer
+    hidden: int
+    max_tokens: int
+    ept: int
+    dtype: torch.dtype
+    num_sf_packs: int
+
+    @property
+    def layers(self) -> int:
+        return len(self.entries)
+
+    @property
+    def element_bytes(self) -> int:
+        return torch.empty((), dtype=self.dtype).element_size()
+
+    @property
+    def row_bytes(self) -> int:
+        return self.hidden * self.element_bytes
+
+    @property
+    def capacity(self) -> int:
+        return self.max_tokens * self.ept
+
+    @property
+    def table_rows(self) -> int:
+        return int(sum(self.entries))
+
+    def table_bases(self):
+        out, at = [], 0
+        for n in self.entries:
+            out.append(at)
+            at += n
+        return out
+
+
+def validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world=None):
+    """Check a configuration and return it as an :class:`EngramConfig`.
+
+    Rules follow the reference's WRITE backend (``buffer.py:111-119,151-156``,
+    ``runtime.cpp:117-145``): BF16 rows take no scales, FP8 e4m3 rows need at
+    least one scale pack, rows are whole 16-byte vectors, and every global row id
+    and flat output position fits the 32-bit indices the kernels use.
+    """
+    entries = tuple(int(n) for n in entries)
+    if not entries or min(entries) < 1 or hidden < 1 or max_tokens < 1 or ept < 1:
+        raise ValueError("Storage dimensions must be positive")
+    if len(entries) > MAX_LAYERS:
+        raise ValueError(f"At most {MAX_LAYERS} layers are supported")
+    if dtype not in (torch.bfloat16, torch.float8_e4m3fn):
+        raise ValueError("Supported vocabulary dtypes: bfloat16 and float8_e4m3fn")
+    if (dtype == torch.float8_e4m3fn) != (num_sf_packs > 0):
+        raise ValueError("FP8 requires scales; BF16 requires num_sf_packs=0")
+    cfg = EngramConfig(entries, int(hidden), int(max_tokens), int(ept), dtype, int(num_sf_packs))
+    if cfg.row_bytes % 16:
+        raise ValueError("A vocabulary row must be a multiple of 16 bytes")
+    if cfg.capacity * cfg.layers >= 2**32:
+        raise ValueError("max_tokens * ept * layers must fit in 32 bits")
+    if cfg.table_rows >= 2**32:
+        raise ValueError("Local vocabulary exceeds 2^32 rows")
+    if world is not None:
+        if not 1 <= world <= MAX_RANKS:
+            raise ValueError(f"World size must be in [1, {MAX_RANKS}]")
+        if any(n * world > 2**31 - 1 for n in entries):
+            raise ValueError("Global row ids must fit in int32")
+    return cfg
+
+
+@dataclass
+class MemoryPlan:
+    """Byte offsets of every region, for one rank of a ``world``-rank buffer."""
+
+    config: EngramConfig
+    world: int
+    mirror: bool
+    local_sf: bool
+    device: dict = field(default_factory=dict)
+    host: dict = field(default_factory=dict)
+    device_bytes: int = 0
+    host_bytes: int = 0
+    sf_bases: list = field(default_factory=list)
+    sf_rows_per_layer: list = field(default_factory=list)
+
+    def as_native(self) -> dict:
+        """Flat dict handed to the C++ runtime (all ints)."""
+        out = {f"dev_{k}": int(v[0]) for k, v in self.device.items()}
+        out.update({f"dev_{k}_bytes": int(v[1]) for k, v in self.device.items()})
+        out.update({f"host_{k}": int(v[0]) for k, v in self.host.items()})
+        out.update({f"host_{k}_bytes": int(v[1]) for k, v in self.host.items()})
+        out["device_bytes"] = int(self.device_bytes)
+        out["host_bytes"] = int(self.host_bytes)
+        return out
+
+
+def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) -> MemoryPlan:
+    """Lay out one rank's host shard and device arena.
+
+    ``mirror``: keep an HBM copy of the vocabulary for the peer-HBM route.
+    ``local_sf``: every rank holds the full global FP8 scale table
+    (``ENGRAM_WRITE_LOCAL_SF=1``); otherwise each rank holds the scales of its own
+    rows only (on one NVLink node that is the node-local shard of the reference,
+    ``runtime.cpp:114-121``).
+    """
+    c = config
+    L, W, P = c.layers, world, c.num_sf_packs
+    plan = MemoryPlan(config=c, world=W, mirror=mirror, local_sf=local_sf)
+
+    sf_rows_per_layer = [n * (W if local_sf else 1) for n in c.entries]
+    sf_bases, at = [], 0
+    for rows in sf_rows_per_layer:
+        sf_bases.append(at)
+        at += rows * P
+    plan.sf_bases, plan.sf_rows_per_layer = sf_bases, sf_rows_per_layer
+    sf_floats = at
+
+    regions = [
+        ("mirror", c.table_rows * c.row_bytes if mirror else 0),
+        ("sf_table", sf_floats * 4),
+        ("output", L * c.capacity * c.row_bytes),
+        ("sf_output", L * align(c.max_tokens, 4) * c.ept * P * 4),
+        ("done", L * W * 8),
+        ("inbox", W * L * c.capacity * 8),
+        # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32,
+        # layer_arrivals[L] u32, push_arrivals[W*L] u32, push_epochs[W*L] u64
+        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + W * L * 4 + W * L * 8 + 256),
+    ]
+    off = 0
+    for name, size in regions:
+        plan.device[name] = (off, size)
+        off = align(off + max(size, 0), REGION_ALIGN)
+    plan.device_bytes = align(max(off, REGION_ALIGN), ALLOC_ALIGN)
+
+    off = 0
+    for name, size in [("table", c.table_rows * c.row_bytes), ("headers", W * L * HEADER_BYTES)]:
+        plan.host[name] = (off, size)
+        off = align(off + size, REGION_ALIGN)
+    plan.host_bytes = align(off, ALLOC_ALIGN)
+    return plan
+
+
+def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf):
+    cfg = validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world)
+    plan = plan_memory(cfg, world, mirror, local_sf)
+    return plan.device_bytes, plan.host_bytes
+
+
+def sf_strides(tokens: int, ept: int, packs: int, col_major: bool):
+    """Strides of one layer's scale output ``[tokens, ept * packs]`` (fp32 units).
+
+    Column-major is TMA aligned: token stride 1, column stride ``align(tokens, 4)``
+    (reference ``runtime.cpp:430-432``).  Returns
+    ``(token_stride, column_stride, layer_stride)``.
+    """
+    if col_major:
+        hs = align(tokens, 4)
+        return 1, hs, hs * ept * packs
+    return ept * packs, 1, tokens * ept * packs

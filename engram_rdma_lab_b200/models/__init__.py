@@ -1,0 +1,23 @@
+from .engram_tables import (
+    CONFIGS,
+    TableSpec,
+    expected_outputs,
+    make_indices,
+    normal_bf16_shard,
+    pattern_scales,
+    pattern_shard,
+    quantized_fp8_shard,
+    row_pattern,
+)
+
+__all__ = [
+    "CONFIGS",
+    "TableSpec",
+    "expected_outputs",
+    "make_indices",
+    "normal_bf16_shard",
+    "pattern_scales",
+    "pattern_shard",
+    "quantized_fp8_shard",
+    "row_pattern",
+]

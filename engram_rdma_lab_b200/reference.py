@@ -1,0 +1,273 @@
+"""Pure-torch EngramBuffer: the correctness oracle and the NCCL baseline.
+
+Same public API as :class:`engram_rdma_lab_b200.EngramBuffer`, built only from
+torch tensor ops and ``torch.distributed`` collectives:
+
+1. bucket every requested row by owner (``x // n_l``), padding last;
+2. ``all_to_all_single`` of per-owner counts, then of ``(layer, local_row)``
+   requests;
+3. each owner gathers the requested rows and FP8 scales from its shard;
+4. ``all_to_all_single`` of rows and scales back;
+5. scatter into the per-layer output region; padding rows and scales are zero.
+
+On CPU with a ``gloo`` group it is the oracle of the unit tests.  On GPUs with
+an ``nccl`` group it is the "NCCL all_to_all" baseline the fused kernels are
+measured against.  The baseline has to read the counts back to the host to size
+the exchange, so every fetch synchronises the host once; the native buffer never
+does.  Reference semantics reproduced: ``sge_write/engram_sge_write/buffer.py``
+(API, validation, hook generations), ``sge_write/csrc/runtime.cpp:389-535``
+(storage, scale sharding, output and scale layouts).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .base import EngramBufferBase, accept_legacy_storage_size
+from .layout import plan_memory, sf_strides, storage_size_hint
+from .routing import EgmConfig, env_flag, node_identity, node_layout, route_names, legacy_route_names, OwnerRoute
+
+
+def _group_device(group, device):
+    if device is not None:
+        return torch.device(device)
+    backend = dist.get_backend(group)
+    if backend == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
+class TorchEngramBuffer(EngramBufferBase):
+    """EngramBuffer implemented with torch collectives (oracle / baseline)."""
+
+    impl_name = "torch"
+
+    @accept_legacy_storage_size
+    def __init__(
+        self,
+        group,
+        num_gpu_bytes,
+        num_rdma_storage_bytes,
+        use_cpu_rdma_storage=True,
+        num_allocated_qps=1,
+        qp_depth=1024,
+        restrict_rd_atomic=False,
+        allow_hybrid_mode=True,
+        sl_idx=None,
+        num_gpu_timeout_secs=100,
+        explicitly_destroy=False,
+        device=None,
+    ):
+        super().__init__(group, explicitly_destroy)
+        if not 1 <= num_allocated_qps <= 16 or qp_depth < 32:
+            raise ValueError("num_allocated_qps must be in [1, 16] and qp_depth >= 32")
+        self.egm = EgmConfig.from_env()
+        self.local_sf = env_flag("ENGRAM_WRITE_LOCAL_SF", self.egm.enabled)
+        self.device = _group_device(group, device)
+        self.num_gpu_bytes, self.num_rdma_storage_bytes = int(num_gpu_bytes), int(num_rdma_storage_bytes)
+        self.use_cpu_rdma_storage = bool(use_cpu_rdma_storage)
+        self.allow_hybrid_mode = bool(allow_hybrid_mode)
+        self.num_allocated_qps, self.qp_depth = int(num_allocated_qps), int(qp_depth)
+        self.restrict_rd_atomic, self.sl_idx = restrict_rd_atomic, sl_idx
+        self.num_gpu_timeout_secs = num_gpu_timeout_secs
+        nodes = [None] * self.num_ranks
+        dist.all_gather_object(nodes, node_identity(), group=group)
+        self.scaleup_rank_idx, self.num_scaleup_ranks = node_layout(nodes, self.rank_idx)
+        self.num_scaleout_ranks = self.num_ranks // self.num_scaleup_ranks
+        self.scaleout_rank_idx = self.rank_idx // self.num_scaleup_ranks
+        self.runtime = self
+
+    # ------------------------------------------------------------ static helpers
+    @staticmethod
+    def get_storage_size_hint(
+        group, num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype=torch.bfloat16,
+        num_sf_packs=0,
+    ):
+        egm = EgmConfig.from_env().enabled
+        return storage_size_hint(
+            num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype, num_sf_packs,
+            group.size(), egm, env_flag("ENGRAM_WRITE_LOCAL_SF", egm),
+        )
+
+    @staticmethod
+    def get_theoretical_config(group, num_layers, num_max_tokens, num_entries_per_token,
+                               num_max_read_requests_per_qp=16):
+        from .buffer import theoretical_config
+
+        return theoretical_config(group.size(), num_layers, num_max_tokens, num_entries_per_token,
+                                  num_max_read_requests_per_qp)
+
+    # ------------------------------------------------------------------ config
+    def set_config(self, num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token,
+                   dtype=torch.bfloat16, num_sf_packs=0):
+        cfg = self._check_config_args(num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype,
+                                      num_sf_packs)
+        plan = plan_memory(cfg, self.num_ranks, self.egm.enabled, self.local_sf)
+        if plan.device_bytes > self.num_gpu_bytes or plan.host_bytes > self.num_rdma_storage_bytes:
+            raise ValueError("Insufficient capacity: use get_storage_size_hint")
+        mine = (tuple(cfg.entries), cfg.hidden, cfg.max_tokens, cfg.ept, str(cfg.dtype), cfg.num_sf_packs,
+                self.egm.enabled, self.local_sf)
+        everyone = [None] * self.num_ranks
+        dist.all_gather_object(everyone, mine, group=self.group)
+        if any(other != mine for other in everyone):
+            raise ValueError("All ranks must use identical configurations")
+        self._config, self._plan = cfg, plan
+        dev = self.device
+        self._table = torch.zeros(cfg.table_rows, cfg.row_bytes, dtype=torch.uint8, device=dev)
+        self._table_bases = torch.tensor(cfg.table_bases(), dtype=torch.int64, device=dev)
+        self._entries_t = torch.tensor(cfg.entries, dtype=torch.int64, device=dev)
+        P = cfg.num_sf_packs
+        total_sf = sum(plan.sf_rows_per_layer)
+        self._sf_table = torch.zeros(max(total_sf, 1), max(P, 1), dtype=torch.float32, device=dev)
+        self._sf_bases = torch.tensor([b // max(P, 1) for b in plan.sf_bases], dtype=torch.int64, device=dev)
+        self._output = torch.zeros(cfg.layers, cfg.capacity, cfg.row_bytes, dtype=torch.uint8, device=dev)
+        self._sf_output = torch.zeros(max(plan.device["sf_output"][1] // 4, 1), dtype=torch.float32, device=dev)
+        self.routes = [OwnerRoute.PEER_HBM if self.egm.enabled else OwnerRoute.HOST] * self.num_ranks
+        self.owner_fallback_reasons = [""] * self.num_ranks
+        self._configured = True
+        dist.barrier(group=self.group)
+
+    def write(self, storages, sfs=None):
+        dev_index = self.device.index if self.device.type == "cuda" else None
+        self._check_write_args(storages, sfs, dev_index)
+        c = self._config
+        dist.barrier(group=self.group)
+        bases = c.table_bases()
+        for layer, n in enumerate(c.entries):
+            src = storages[layer].reshape(n, c.hidden).view(torch.uint8).reshape(n, c.row_bytes)
+            self._table[bases[layer]:bases[layer] + n].copy_(src)
+            if c.num_sf_packs:
+                sf = sfs[layer]
+                rows = self._plan.sf_rows_per_layer[layer]
+                start = 0 if self.local_sf else self.rank_idx * n
+                base = self._plan.sf_bases[layer] // c.num_sf_packs
+                self._sf_table[base:base + rows].copy_(sf[start:start + rows])
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._written = True
+
+    # ------------------------------------------------------------------- fetch
+    def fetch(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
+        """Exchange requests and rows with all_to_all; returns one hook per layer."""
+        dev_index = self.device.index if self.device.type == "cuda" else None
+        self._check_fetch_args(indices, dev_index, require_cuda=self.device.type == "cuda")
+        if self.device.type != "cuda" and indices.device.type != "cpu":
+            raise ValueError("indices must live on the buffer's device")
+        qps = num_qps or self.num_allocated_qps
+        if not 1 <= qps <= self.num_allocated_qps:
+            raise ValueError("num_qps exceeds the allocated channels")
+        generation = self._begin_fetch()
+        self._input = indices
+        outputs = self._exchange(indices, use_tma_aligned_col_major_sf)
+        return self._make_hooks(generation, lambda layer: None, outputs)
+
+    def _exchange(self, indices, col_major):
+        c, W, dev = self._config, self.num_ranks, self.device
+        L, T, E = indices.shape
+        P, R = c.num_sf_packs, c.row_bytes
+        rows = T * E
+        x = indices.reshape(L, rows).to(torch.int64)
+        valid = x >= 0
+        n = self._entries_t[:, None]
+        owner = torch.where(valid, torch.div(x.clamp_min(0), n, rounding_mode="floor"), torch.full_like(x, W))
+        if bool((owner[valid] >= W).any()) if valid.any() else False:
+            raise ValueError("index outside the global vocabulary")
+        local = torch.where(valid, x.clamp_min(0) % n, torch.zeros_like(x))
+        layer_ids = torch.arange(L, device=dev, dtype=torch.int64)[:, None].expand(L, rows)
+        positions = torch.arange(L * rows, device=dev, dtype=torch.int64)
+        owner_f, local_f, layer_f = owner.reshape(-1), local.reshape(-1), layer_ids.reshape(-1)
+        order = torch.sort(owner_f, stable=True).indices
+        send_counts = torch.bincount(owner_f, minlength=W + 1)[:W]
+        total = int(send_counts.sum())  # host sync: the baseline must size its buffers
+        keep = order[:total]
+        request = (layer_f[keep] << 32) | local_f[keep]
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        send_split, recv_split = send_counts.tolist(), recv_counts.tolist()
+        incoming = torch.empty(sum(recv_split), dtype=torch.int64, device=dev)
+        dist.all_to_all_single(incoming, request, recv_split, send_split, group=self.group)
+
+        # Owner side: serve rows and scales from this rank's shard.
+        in_layer, in_row = incoming >> 32, incoming & 0xFFFFFFFF
+        served = self._table[self._table_bases[in_layer] + in_row]
+        answer = torch.empty(total, R, dtype=torch.uint8, device=dev)
+        dist.all_to_all_single(answer, served.contiguous(), send_split, recv_split, group=self.group)
+        if P:
+            sf_off = self._entries_t[in_layer] * self.rank_idx if self.local_sf else torch.zeros_like(in_row)
+            served_sf = self._sf_table[self._sf_bases[in_layer] + sf_off + in_row]
+            answer_sf = torch.empty(total, P, dtype=torch.float32, device=dev)
+            dist.all_to_all_single(answer_sf, served_sf.contiguous(), send_split, recv_split, group=self.group)
+
+        # Requester side: scatter into the output region; padding stays zero.
+        out = self._output[:, :rows]
+        out.zero_()
+        flat_out = self._output.view(L * c.capacity, R)
+        dst = (positions[keep] // rows) * c.capacity + positions[keep] % rows
+        flat_out[dst] = answer
+        results = []
+        dtype = c.dtype
+        if P:
+            ts, hs, ls = sf_strides(T, E, P, col_major)
+            sf_rows = torch.zeros(L * rows, P, dtype=torch.float32, device=dev)
+            sf_rows[positions[keep]] = answer_sf
+            for layer in range(L):
+                view = self._sf_output.as_strided((T, E * P), (ts, hs), layer * ls)
+                view.copy_(sf_rows[layer * rows:(layer + 1) * rows].reshape(T, E * P))
+        for layer in range(L):
+            data = self._output[layer, :rows].view(dtype).reshape(T, E * c.hidden)
+            if P:
+                ts, hs, ls = sf_strides(T, E, P, col_major)
+                results.append((data, self._sf_output.as_strided((T, E * P), (ts, hs), layer * ls)))
+            else:
+                results.append(data)
+        return results
+
+    # -------------------------------------------------------------- inspection
+    def get_route_info(self):
+        self._ready()
+        return dict(
+            egm_enabled=self.egm.enabled,
+            owner_routes=route_names(self.routes),
+            owner_routes_legacy=legacy_route_names(self.routes),
+            owner_fallback_reasons=list(self.owner_fallback_reasons),
+            fabric_domain=None,
+            fabric_probe_error="disabled",
+            transport="torch.distributed all_to_all",
+            memory=self.memory_usage(),
+        )
+
+    def memory_usage(self):
+        c = self._config
+        return dict(
+            rank=self.rank_idx,
+            impl=self.impl_name,
+            device_bytes=self._plan.device_bytes,
+            host_bytes=self._plan.host_bytes,
+            cpu_vocabulary_bytes=c.table_rows * c.row_bytes,
+            local_sf=self.local_sf,
+            egm_enabled=self.egm.enabled,
+        )
+
+    def print_memory_usage(self):
+        self._ready()
+        print(self.memory_usage(), flush=True)
+
+    def get_physical_domain_size(self):
+        return self.num_scaleout_ranks, self.num_scaleup_ranks
+
+    def get_logical_domain_size(self):
+        return self.num_scaleout_ranks, self.num_scaleup_ranks
+
+    def destroy(self):
+        self._check_destroy()
+        if self._destroyed:
+            return
+        if self._configured:
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        self._destroyed = True
+        self._input = None
+        self._table = self._output = self._sf_table = self._sf_output = None

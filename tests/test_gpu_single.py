@@ -1,0 +1,197 @@
+"""EngramBuffer on one B200 (world_size=1): the gather kernel end to end.
+
+Every output is compared bit-exactly with the pattern oracle or with plain
+torch indexing of the written tables.
+"""
+
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+
+from engram_rdma_lab_b200 import EngramBuffer
+from engram_rdma_lab_b200.models import expected_outputs, make_indices, pattern_shard
+
+from .conftest import free_port
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def world1():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    torch.cuda.set_device(0)
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{free_port()}")
+    yield
+    # Leave the group for the rest of the session.
+
+
+def make_buffer(entries, hidden, max_tokens, ept, dtype, packs, egm, local_sf=None, timeout=20):
+    os.environ["ENGRAM_EGM_ENABLE"] = "1" if egm else "0"
+    if local_sf is None:
+        os.environ.pop("ENGRAM_WRITE_LOCAL_SF", None)
+    else:
+        os.environ["ENGRAM_WRITE_LOCAL_SF"] = "1" if local_sf else "0"
+    group = dist.group.WORLD
+    sizes = EngramBuffer.get_storage_size_hint(group, entries, hidden, max_tokens, ept, dtype, packs)
+    cfg = EngramBuffer.get_theoretical_config(group, len(entries), max_tokens, ept)
+    buf = EngramBuffer(group, *sizes, True, *cfg, num_gpu_timeout_secs=timeout, explicitly_destroy=True)
+    buf.set_config(entries, hidden, max_tokens, ept, dtype, packs)
+    return buf
+
+
+def check(outputs, indices, entries, hidden, dtype, packs, salt=0, col_major=True):
+    exp = expected_outputs(indices.cpu(), entries, hidden, dtype, packs, salt)
+    T, E = indices.shape[1], indices.shape[2]
+    for layer, out in enumerate(outputs):
+        data, sf = out if packs else (out, None)
+        assert data.shape == (T, E * hidden) and data.dtype == dtype and data.is_cuda
+        assert torch.equal(data.view(torch.uint8).reshape(T, -1).cpu(), exp[layer][0]), f"layer {layer} data"
+        if packs:
+            assert sf.shape == (T, E * packs)
+            assert sf.stride() == ((1, (T + 3) // 4 * 4) if col_major else (E * packs, 1))
+            assert torch.equal(sf.cpu(), exp[layer][1]), f"layer {layer} scales"
+
+
+@pytest.mark.parametrize("egm", [True, False])
+def test_bf16_gather(egm):
+    entries, hidden, ept = (5000, 7001), 256, 8
+    buf = make_buffer(entries, hidden, 1024, ept, torch.bfloat16, 0, egm)
+    storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+    buf.write(storages)
+    for epoch, tokens in enumerate([1024, 333, 1]):
+        idx = make_indices(0, 1, entries, tokens, ept, epoch=epoch, padding=0.05, device="cuda")
+        hooks = buf.fetch(idx)
+        outs = [None, None]
+        outs[1], outs[0] = hooks[1](), hooks[0]()  # reverse order
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, torch.bfloat16, 0)
+    info = buf.get_route_info()
+    assert info["owner_routes"] == ["peer_hbm" if egm else "host"]
+    mem = info["memory"]
+    assert mem["hbm_mirror_bytes"] == (sum(entries) * hidden * 2 if egm else 0)
+    assert mem["kernel_launches"] >= 3
+    buf.destroy()
+
+
+@pytest.mark.parametrize("local_sf", [True, False])
+@pytest.mark.parametrize("hidden,packs", [(256, 2), (512, 4), (128, 1)])
+def test_fp8_gather_and_scales(local_sf, hidden, packs):
+    entries, ept = (3001, 4099), 24
+    buf = make_buffer(entries, hidden, 512, ept, torch.float8_e4m3fn, packs, True, local_sf)
+    storages, scales = pattern_shard(0, 1, entries, hidden, torch.float8_e4m3fn, packs, "cuda")
+    buf.write(storages, scales)
+    for col_major in (True, False):
+        idx = make_indices(0, 1, entries, 509, ept, epoch=7, padding=0.03, device="cuda")
+        outs = [h() for h in buf.fetch(idx, use_tma_aligned_col_major_sf=col_major)]
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, torch.float8_e4m3fn, packs, col_major=col_major)
+    buf.destroy()
+
+
+def test_matches_plain_torch_indexing_with_cpu_weights():
+    entries, hidden, ept = (4096, 4100), 64, 4
+    buf = make_buffer(entries, hidden, 256, ept, torch.bfloat16, 0, False)
+    g = torch.Generator().manual_seed(3)
+    tables = [(torch.randn(n, hidden, generator=g) * 0.02).to(torch.bfloat16) for n in entries]
+    buf.write(tables)  # CPU tensors
+    idx = make_indices(0, 1, entries, 256, ept, padding=0.1, device="cuda")
+    outs = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    for layer, table in enumerate(tables):
+        x = idx[layer].cpu().long()
+        ref = table.float()[x.clamp_min(0)] * (x >= 0)[..., None]
+        assert torch.equal(outs[layer].cpu().float().reshape(256, ept, hidden), ref)
+    buf.destroy()
+
+
+def test_zero_tokens_and_capacity_checks():
+    entries, hidden, ept = (100, 200), 64, 3
+    buf = make_buffer(entries, hidden, 16, ept, torch.bfloat16, 0, True)
+    storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+    buf.write(storages)
+    outs = [h() for h in buf.fetch(torch.empty(2, 0, ept, dtype=torch.int32, device="cuda"))]
+    assert all(o.shape == (0, ept * hidden) for o in outs)
+    with pytest.raises(ValueError):
+        buf.fetch(torch.zeros(2, 17, ept, dtype=torch.int32, device="cuda"))  # over capacity
+    with pytest.raises(ValueError):
+        buf.fetch(torch.zeros(2, 4, ept, dtype=torch.int32))  # CPU indices
+    buf.destroy()
+
+
+def test_cuda_graph_replay_and_cross_stream_hooks():
+    entries, hidden, ept = (9000, 9001), 256, 24
+    buf = make_buffer(entries, hidden, 256, ept, torch.float8_e4m3fn, 2, True)
+    storages, scales = pattern_shard(0, 1, entries, hidden, torch.float8_e4m3fn, 2, "cuda")
+    buf.write(storages, scales)
+    idx = make_indices(0, 1, entries, 256, ept, padding=0.02, device="cuda")
+    side = torch.cuda.Stream()
+    for _ in range(2):  # warm up outside the graph
+        outs = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n = torch.tensor(entries, device="cuda", dtype=torch.int32)[:, None, None]
+    with torch.cuda.graph(graph):
+        idx.add_(7).remainder_(n)  # the producer is part of the graph
+        hooks = buf.fetch(idx)
+        outs = [None, None]
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            outs[1] = hooks[1]()
+            outs[0] = hooks[0]()
+        torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, torch.float8_e4m3fn, 2)
+    # Eager fetch after the graph still works and waits for the graph's layers.
+    more = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    check(more, idx, entries, hidden, torch.float8_e4m3fn, 2)
+    del graph
+    buf.destroy()
+
+
+def test_out_of_range_index_reports_error():
+    entries, hidden, ept = (64, 64), 64, 2
+    buf = make_buffer(entries, hidden, 8, ept, torch.bfloat16, 0, True)
+    storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+    buf.write(storages)
+    idx = torch.zeros(2, 8, ept, dtype=torch.int32, device="cuda")
+    idx[1, 3, 1] = 64 * 5  # beyond the single rank's vocabulary
+    outs = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    assert outs[1][3].view(torch.uint8).sum().item() == 0  # zero-filled, not trapped
+    state = buf.error_state()
+    assert state["status"] == 2 and state["layer"] == 1
+    with pytest.raises(RuntimeError, match="outside the vocabulary"):
+        buf.fetch(idx)
+    buf._pending = set()
+    buf.destroy()
+
+
+def test_bounded_wait_times_out_without_fault():
+    entries, hidden, ept = (64,), 64, 2
+    buf = make_buffer(entries, hidden, 8, ept, torch.bfloat16, 0, True)
+    result = buf.runtime.run_wait_probe(200.0)
+    assert result["status"] == 1  # timeout reported
+    assert result["elapsed_ms"] >= 150
+    # The context is still usable.
+    storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+    buf.write(storages)
+    idx = make_indices(0, 1, entries, 8, ept, device="cuda")
+    outs = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    check(outs, idx, entries, hidden, torch.bfloat16, 0)
+    buf.destroy()
+
+
+def test_native_extension_is_in_tree():
+    from engram_rdma_lab_b200 import _native
+
+    mod = _native.load()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    assert os.path.realpath(mod.__file__).startswith(os.path.realpath(root))

@@ -1,0 +1,147 @@
+"""Configuration checks, memory plan, synthetic tables and index streams (host only)."""
+
+import pytest
+import torch
+
+from engram_rdma_lab_b200.buffer import theoretical_config
+from engram_rdma_lab_b200.layout import (
+    ALLOC_ALIGN,
+    REGION_ALIGN,
+    plan_memory,
+    sf_strides,
+    storage_size_hint,
+    validate_config,
+)
+from engram_rdma_lab_b200.models import (
+    CONFIGS,
+    expected_outputs,
+    make_indices,
+    pattern_scales,
+    pattern_shard,
+    row_pattern,
+)
+from engram_rdma_lab_b200.ops import dequantize_fp8_blockwise, quantize_fp8_blockwise
+
+
+def test_validate_config_rules():
+    validate_config([10, 11], 64, 8, 2, torch.bfloat16, 0, world=2)
+    with pytest.raises(ValueError):
+        validate_config([10], 64, 8, 2, torch.bfloat16, 2)  # BF16 takes no scales
+    with pytest.raises(ValueError):
+        validate_config([10], 64, 8, 2, torch.float8_e4m3fn, 0)  # FP8 needs scales
+    with pytest.raises(ValueError):
+        validate_config([10], 12, 8, 2, torch.float8_e4m3fn, 1)  # 12 B rows
+    with pytest.raises(ValueError):
+        validate_config([10], 64, 8, 2, torch.float32, 0)
+    with pytest.raises(ValueError):
+        validate_config([], 64, 8, 2, torch.bfloat16, 0)
+    with pytest.raises(ValueError):
+        validate_config([0], 64, 8, 2, torch.bfloat16, 0)
+    with pytest.raises(ValueError):
+        validate_config([2**30], 64, 8, 2, torch.bfloat16, 0, world=4)  # global ids overflow int32
+    with pytest.raises(ValueError):
+        validate_config([1] * 33, 64, 8, 2, torch.bfloat16, 0)
+
+
+@pytest.mark.parametrize("mirror", [False, True])
+@pytest.mark.parametrize("local_sf", [False, True])
+def test_plan_regions_disjoint_and_aligned(mirror, local_sf):
+    cfg = validate_config([524288, 524309], 256, 4096, 24, torch.float8_e4m3fn, 2, world=8)
+    plan = plan_memory(cfg, 8, mirror, local_sf)
+    spans = sorted((off, off + size) for off, size in plan.device.values())
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 <= b0
+    assert all(off % REGION_ALIGN == 0 for off, _ in plan.device.values())
+    assert plan.device_bytes % ALLOC_ALIGN == 0 and plan.host_bytes % ALLOC_ALIGN == 0
+    assert plan.device["mirror"][1] == (cfg.table_rows * 256 if mirror else 0)
+    assert plan.device["output"][1] == 2 * 4096 * 24 * 256
+    assert plan.host["table"][1] == cfg.table_rows * 256
+    sf_rows = sum(n * (8 if local_sf else 1) for n in cfg.entries)
+    assert plan.device["sf_table"][1] == sf_rows * 2 * 4
+    assert storage_size_hint([524288, 524309], 256, 4096, 24, torch.float8_e4m3fn, 2, 8, mirror, local_sf) == (
+        plan.device_bytes, plan.host_bytes)
+
+
+def test_sf_strides():
+    assert sf_strides(5, 3, 2, True) == (1, 8, 8 * 6)
+    assert sf_strides(5, 3, 2, False) == (6, 1, 30)
+    assert sf_strides(0, 3, 2, True) == (1, 0, 0)
+
+
+def test_theoretical_config():
+    ch, depth, restrict = theoretical_config(8, 2, 4096, 24)
+    assert 1 <= ch <= 16 and depth >= 1024 and restrict is False
+    with pytest.raises(ValueError):
+        theoretical_config(8, 0, 4096, 24)
+
+
+def test_row_pattern_deterministic_and_distinct():
+    rows = torch.arange(64)
+    a = row_pattern(rows, 0, 256)
+    assert a.shape == (64, 256) and a.dtype == torch.uint8
+    assert torch.equal(a, row_pattern(rows, 0, 256))
+    assert not torch.equal(a, row_pattern(rows, 1, 256))
+    assert len({bytes(r.tolist()) for r in a}) == 64
+
+
+def test_pattern_shard_matches_expected():
+    world, entries, hidden = 3, (7, 9), 16
+    shards = [pattern_shard(r, world, entries, hidden, torch.float8_e4m3fn, 2, "cpu") for r in range(world)]
+    idx = torch.tensor([[[0, 20, -1], [5, 13, 2]], [[26, 0, 9], [-1, -1, 17]]], dtype=torch.int32)
+    exp = expected_outputs(idx, entries, hidden, torch.float8_e4m3fn, 2)
+    for layer, n in enumerate(entries):
+        flat = idx[layer].reshape(-1)
+        for i, x in enumerate(flat.tolist()):
+            got = exp[layer][0].reshape(-1, hidden)[i]
+            sf = exp[layer][1].reshape(-1, 2)[i]
+            if x < 0:
+                assert got.sum() == 0 and sf.sum() == 0
+            else:
+                owner, local = divmod(x, n)
+                assert torch.equal(got, shards[owner][0][layer][local].view(torch.uint8))
+                assert torch.equal(sf, shards[owner][1][layer][x])
+    sc = pattern_scales(torch.arange(1000), 0, 2)
+    assert float(sc.min()) >= 2**-8 and float(sc.max()) <= 1.0
+    assert torch.all(torch.log2(sc) == torch.round(torch.log2(sc)))
+
+
+def test_make_indices_distributions():
+    world, entries = 4, (100, 103)
+    u = make_indices(0, world, entries, 64, 6, distribution="uniform")
+    assert u.shape == (2, 64, 6) and u.dtype == torch.int32
+    assert int(u[0].max()) < world * 100 and int(u[1].max()) < world * 103 and int(u.min()) >= 0
+    o = make_indices(1, world, entries, 64, 6, owner=2)
+    for layer, n in enumerate(entries):
+        assert torch.all(o[layer] // n == 2)
+    s = make_indices(0, world, entries, 64, 6, distribution="stratified")
+    interval = world * 100 // 6
+    assert torch.all(s[0] // interval == torch.arange(6))
+    p = make_indices(0, world, entries, 512, 6, padding=0.1)
+    frac = float((p < 0).float().mean())
+    assert 0.05 < frac < 0.15
+    z = make_indices(0, world, entries, 2048, 6, distribution="zipf")
+    owners = (z[0].long() // 100).flatten()
+    counts = torch.bincount(owners, minlength=world)
+    assert counts[0] > counts[-1]  # low ids are hot
+    m1 = make_indices(3, world, entries, 16, 6, distribution="matched", epoch=2)
+    m2 = make_indices(3, world, entries, 16, 6, distribution="matched", epoch=2)
+    assert torch.equal(m1, m2)
+    assert not torch.equal(m1, make_indices(3, world, entries, 16, 6, distribution="matched", epoch=3))
+
+
+def test_configs_shapes():
+    assert CONFIGS["fp8"].bytes_per_fetch() == 2 * 4096 * 24 * 256
+    assert CONFIGS["fp8_graph"].row_bytes == 512
+    assert CONFIGS["oracle"].layers == 2
+
+
+def test_fp8_roundtrip():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(32, 256, generator=g)
+    codes, scales = quantize_fp8_blockwise(x)
+    assert codes.dtype == torch.float8_e4m3fn and scales.shape == (32, 2)
+    back = dequantize_fp8_blockwise(codes, scales, dtype=torch.float32)
+    rel = (back - x).abs().max() / x.abs().max()
+    assert rel < 0.07  # e4m3 has a 3-bit mantissa
+    codes2, scales2 = quantize_fp8_blockwise(x, power_of_two=True)
+    assert torch.all(torch.log2(scales2) == torch.round(torch.log2(scales2)))
