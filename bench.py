@@ -145,8 +145,10 @@ def main():
             step(graph_idx)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
+        before = buf.runtime.memory_usage()["kernel_launches"] if native else 0
         with torch.cuda.graph(graph):
             step(graph_idx)
+        graph_launches = (buf.runtime.memory_usage()["kernel_launches"] - before) if native else 0
 
     def run(k):
         if graph is None:
@@ -185,6 +187,8 @@ def main():
     if sampler:
         sampler.__exit__(None, None, None)
     launches = (buf.runtime.memory_usage()["kernel_launches"] - launches_before) if native else 0
+    if graph is not None:
+        launches = graph_launches * args.steps  # kernels replayed from the captured graph
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     all_ms = gather_floats(step_ms)
     per_step_max = [max(r[k] for r in all_ms) for k in range(args.steps)]

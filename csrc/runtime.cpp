@@ -491,6 +491,13 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         return d;
     }
 
+    // Fault injection for tests: stop serving requesters, as a dead owner
+    // process would.  Requesters then see their bounded hook wait run out.
+    void debug_stop_service() {
+        py::gil_scoped_release release;
+        service_.stop_and_join();
+    }
+
     void close() {
         if (closed_)
             return;
@@ -850,6 +857,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("memory_usage", &Runtime::memory_usage)
         .def("debug_state", &Runtime::debug_state)
         .def("run_wait_probe", &Runtime::run_wait_probe)
+        .def("debug_stop_service", &Runtime::debug_stop_service)
         .def("close", &Runtime::close)
         .def_property_readonly("closed", &Runtime::closed);
     py::class_<OwnerServiceHarness>(m, "OwnerServiceHarness")

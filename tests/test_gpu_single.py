@@ -162,11 +162,12 @@ def test_out_of_range_index_reports_error():
     buf.write(storages)
     idx = torch.zeros(2, 8, ept, dtype=torch.int32, device="cuda")
     idx[1, 3, 1] = 64 * 5  # beyond the single rank's vocabulary
-    outs = [h() for h in buf.fetch(idx)]
-    torch.cuda.synchronize()
-    assert outs[1][3].view(torch.uint8).sum().item() == 0  # zero-filled, not trapped
+    hooks = buf.fetch(idx)
+    torch.cuda.synchronize()  # the kernel has reported by now
     state = buf.error_state()
-    assert state["status"] == 2 and state["layer"] == 1
+    assert state["status"] == 2 and state["layer"] == 1 and state["owner"] == 5
+    with pytest.raises(RuntimeError, match="outside the vocabulary"):
+        hooks[0]()  # hooks re-raise the latched device error
     with pytest.raises(RuntimeError, match="outside the vocabulary"):
         buf.fetch(idx)
     buf._pending = set()
