@@ -5,17 +5,21 @@
 // (`issue_egm`, WRITE).  Differences by design:
 //   * the source of a direct row is the owner's HBM mirror reached through
 //     NVLink 5 / NVSwitch (or this rank's own shard), not host memory over C2C;
+//   * rows move with TMA bulk copies (`cp.async.bulk` global -> shared, one
+//     per row, completing on an mbarrier) into an 8-stage shared-memory ring,
+//     so a single producer lane keeps hundreds of rows in flight per SM
+//     without holding registers; a consumer warp streams finished stages to
+//     the final [tokens, hidden*ept] positions, zero-filling padding rows;
+//   * dedicated warps gather the FP8 scales with several independent loads in
+//     flight per lane, writing the column-major layout coalesced;
 //   * route tables, layer geometry and strides are kernel parameters
-//     (__grid_constant__), so CUDA Graph replays carry them without any
-//     device-side metadata upload;
-//   * every lane keeps several independent 16-byte loads in flight (UNROLL
-//     rows per lane) so that ~10 MB of requests are outstanding GPU-wide, far
-//     above the NVLink bandwidth-delay product, and stores go straight to the
-//     final [tokens, hidden*ept] position (no reorder pass);
-//   * an out-of-range index is recorded in the error record and zero-filled
-//     instead of trapping.
-// Loads from peer memory are plain per-thread vector loads: no TMA and no
-// cluster multicast touches another GPU's memory.
+//     (__grid_constant__), so CUDA Graph replays carry them;
+//   * an out-of-range index is recorded in the error record and zero-filled,
+//     and every barrier wait is bounded; nothing traps.
+// The bulk copies are plain (non-multicast) loads; reading a peer's memory
+// this way is allowed, multicast from peer memory never appears here.
+// A SIMT variant (16-byte vector loads, ENGRAM_GATHER_KERNEL=simt) is kept for
+// rows too large for the shared-memory ring and for A/B measurements.
 #include "params.h"
 #include "ptx.cuh"
 
@@ -23,13 +27,68 @@ namespace engram {
 
 namespace {
 
-constexpr int kGatherThreads = 512;
+constexpr int kSimtThreads = 512;
+constexpr int kBulkTile = 32;           // rows per stage: one producer lane per row
+constexpr int kBulkThreads = 128;       // producer warp, consumer warp, 2 scale warps
+constexpr uint32_t kStageTargetBytes = 64 * 1024;
+constexpr uint64_t kPipelineTimeoutNs = 2000000000ull;
 
-template <int LPR, int VPL, int UNROLL>
-__global__ void __launch_bounds__(kGatherThreads, 2) gather_kernel(const __grid_constant__ GatherParams p) {
-    __shared__ uint64_t s_direct[kMaxRanks];
-    __shared__ uint64_t s_sf[kMaxRanks];
-    __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
+struct StageMeta {
+    uint32_t layer, start, count, direct_mask, zero_mask, pad[3];
+};
+
+// Scale warps shared by both variants: `lanes` threads starting at `lane_id`
+// gather the scales of every (layer, row) item, 4 items in flight per lane.
+__device__ __forceinline__ void gather_scales(const GatherParams &p, const uint64_t *s_sf, const uint32_t *s_entries,
+                                              const uint32_t *s_sfbase, uint32_t lane_id, uint32_t lanes) {
+    constexpr int kItems = 4;
+    const uint32_t total = p.layers * p.rows;
+    for (uint32_t base = lane_id; base < total; base += lanes * kItems) {
+        const float *src[kItems];
+        float *out[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const uint32_t item = base + u * lanes;
+            src[u] = nullptr;
+            out[u] = nullptr;
+            if (item >= total)
+                continue;
+            const uint32_t layer = item / p.rows;
+            const uint32_t r = item - layer * p.rows;
+            uint32_t token, slot;
+            if (p.col_major_sf) {
+                slot = r / p.tokens;
+                token = r - slot * p.tokens;
+            } else {
+                token = r / p.ept;
+                slot = r - token * p.ept;
+            }
+            const int32_t x = __ldg(p.indices + layer * p.rows + token * p.ept + slot);
+            out[u] = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
+                     uint64_t(slot) * p.packs * p.sf_hidden_stride;
+            if (x >= 0) {
+                const uint32_t span = s_entries[layer] * p.sf_shard_div;
+                const uint32_t shard = uint32_t(x) / span;
+                if (shard < p.world && s_sf[shard] != 0)
+                    src[u] = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
+                             uint64_t(uint32_t(x) - shard * span) * p.packs;
+            }
+        }
+        for (uint32_t k = 0; k < p.packs; ++k) {
+            float v[kItems];
+#pragma unroll
+            for (int u = 0; u < kItems; ++u)
+                v[u] = src[u] != nullptr ? __ldg(src[u] + k) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kItems; ++u)
+                if (out[u] != nullptr)
+                    out[u][uint64_t(k) * p.sf_hidden_stride] = v[u];
+        }
+    }
+}
+
+__device__ __forceinline__ void load_tables(const GatherParams &p, uint64_t *s_direct, uint64_t *s_sf,
+                                            uint32_t *s_entries, uint32_t *s_tbase, uint32_t *s_sfbase) {
     for (uint32_t i = threadIdx.x; i < p.world; i += blockDim.x) {
         s_direct[i] = p.direct_base[i];
         s_sf[i] = p.sf_base[i];
@@ -39,33 +98,171 @@ __global__ void __launch_bounds__(kGatherThreads, 2) gather_kernel(const __grid_
         s_tbase[i] = p.layer.table_bases[i];
         s_sfbase[i] = p.layer.sf_bases[i];
     }
+}
+
+// ------------------------------------------------------------- TMA variant
+__global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_constant__ GatherParams p,
+                                                                   uint32_t tiles_per_layer, uint32_t tiles_per_cta,
+                                                                   uint32_t stages) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
+    __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
+    const uint32_t stage_bytes = kBulkTile * p.row_bytes;
+    uint8_t *data = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(stages) * stage_bytes);
+    uint64_t *empty = full + stages;
+    StageMeta *meta = reinterpret_cast<StageMeta *>(empty + stages);
+
+    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        fence_mbar_init();
+    }
     __syncthreads();
 
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t num_warps = blockDim.x / 32;
-    const uint32_t row_warps = num_warps - p.sf_warps;
-    const uint64_t total = uint64_t(p.layers) * p.rows;
+    const uint32_t total_tiles = p.layers * tiles_per_layer;
+    const uint32_t t0 = blockIdx.x * tiles_per_cta;
+    const uint32_t t1 = min(t0 + tiles_per_cta, total_tiles);
+
+    if (warp == 0) {
+        // Producer: classify the tile's rows and issue one bulk copy per direct row.
+        auto index_of = [&](uint32_t t, uint32_t &layer, uint32_t &start, uint32_t &count) {
+            layer = t / tiles_per_layer;
+            start = (t - layer * tiles_per_layer) * kBulkTile;
+            count = min(uint32_t(kBulkTile), p.rows - start);
+        };
+        uint32_t layer = 0, start = 0, count = 0;
+        int32_t x_next = -1;
+        if (t0 < t1) {
+            index_of(t0, layer, start, count);
+            x_next = lane < count ? __ldg(p.indices + layer * p.rows + start + lane) : -1;
+        }
+        for (uint32_t t = t0, k = 0; t < t1; ++t, ++k) {
+            const uint32_t stage = k % stages, phase = k / stages;
+            index_of(t, layer, start, count);
+            const int32_t x = x_next;
+            if (t + 1 < t1) {  // prefetch the next tile's indices
+                uint32_t nl, ns, nc;
+                index_of(t + 1, nl, ns, nc);
+                x_next = lane < nc ? __ldg(p.indices + nl * p.rows + ns + lane) : -1;
+            }
+            if (k >= stages && !mbar_wait(empty + stage, (phase - 1) & 1, kPipelineTimeoutNs)) {
+                if (lane == 0)
+                    report_error(p.error, kPipelineTimeout, layer, 0, t, 0);
+                break;
+            }
+            const uint8_t *src = nullptr;
+            bool zero = false;
+            if (lane < count) {
+                if (x < 0) {
+                    zero = true;
+                } else {
+                    const uint32_t n = s_entries[layer];
+                    const uint32_t owner = uint32_t(x) / n;
+                    if (owner >= p.world) {
+                        zero = true;
+                        report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
+                    } else if (s_direct[owner] != 0) {
+                        const uint64_t row = uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n);
+                        src = reinterpret_cast<const uint8_t *>(s_direct[owner]) + row * p.row_bytes;
+                    }
+                }
+            }
+            const uint32_t direct_mask = __ballot_sync(0xFFFFFFFFu, src != nullptr);
+            const uint32_t zero_mask = __ballot_sync(0xFFFFFFFFu, zero);
+            if (lane == 0) {
+                meta[stage] = StageMeta{layer, start, count, direct_mask, zero_mask, {0, 0, 0}};
+                mbar_arrive_expect_tx(full + stage, __popc(direct_mask) * p.row_bytes);
+            }
+            __syncwarp();
+            if (src != nullptr)
+                bulk_load(data + size_t(stage) * stage_bytes + size_t(lane) * p.row_bytes, src, p.row_bytes,
+                          full + stage);
+        }
+    } else if (warp == 1) {
+        // Consumer: stream each finished stage to the output.
+        const uint32_t vectors = p.row_bytes / 16;
+        const uint32_t lpr = vectors < 32 ? vectors : 32;
+        const uint32_t rps = 32 / lpr;
+        const uint32_t sub = lane / lpr, vl = lane % lpr;
+        for (uint32_t t = t0, k = 0; t < t1; ++t, ++k) {
+            const uint32_t stage = k % stages, phase = k / stages;
+            if (!mbar_wait(full + stage, phase & 1, kPipelineTimeoutNs)) {
+                if (lane == 0)
+                    report_error(p.error, kPipelineTimeout, 0, 1, t, 0);
+                break;
+            }
+            const StageMeta m = meta[stage];
+            const uint32_t live = m.direct_mask | m.zero_mask;
+            uint8_t *dst = p.output + (uint64_t(m.layer) * p.capacity + m.start) * p.row_bytes;
+            const uint8_t *src = data + size_t(stage) * stage_bytes;
+            if (sub < rps) {
+                for (uint32_t v = vl; v < vectors; v += lpr) {
+                    for (uint32_t r0 = sub; r0 < m.count; r0 += rps * 4) {
+                        Vec16 val[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const uint32_t r = r0 + u * rps;
+                            val[u] = Vec16{0, 0, 0, 0};
+                            if (r < m.count && ((m.direct_mask >> r) & 1u))
+                                val[u] = ld_shared_v4(src + size_t(r) * p.row_bytes + v * 16);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const uint32_t r = r0 + u * rps;
+                            if (r < m.count && ((live >> r) & 1u))
+                                st_v4(dst + size_t(r) * p.row_bytes + v * 16, val[u]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(empty + stage);
+        }
+    } else if (p.packs > 0) {
+        const uint32_t sf_warps = kBulkThreads / 32 - 2;
+        gather_scales(p, s_sf, s_entries, s_sfbase, blockIdx.x * sf_warps * 32 + (warp - 2) * 32 + lane,
+                      gridDim.x * sf_warps * 32);
+    }
+}
+
+// ------------------------------------------------------------ SIMT variant
+template <int LPR, int VPL, int UNROLL>
+__global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
+    __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
+    __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
+    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
+    __syncthreads();
+
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t row_warps = blockDim.x / 32 - p.sf_warps;
+    const uint32_t total = p.layers * p.rows;
 
     if (warp < row_warps) {
         constexpr uint32_t kRowsPerStep = 32 / LPR;
         constexpr uint32_t kRowsPerIter = kRowsPerStep * UNROLL;
         const uint32_t sub = lane / LPR, vlane = lane % LPR;
         const uint32_t vectors = p.row_bytes / 16;
-        const uint64_t first = (uint64_t(blockIdx.x) * row_warps + warp) * kRowsPerIter;
-        const uint64_t stride = uint64_t(gridDim.x) * row_warps * kRowsPerIter;
-        for (uint64_t base = first; base < total; base += stride) {
+        const uint32_t first = (blockIdx.x * row_warps + warp) * kRowsPerIter;
+        const uint32_t stride = gridDim.x * row_warps * kRowsPerIter;
+        for (uint32_t base = first; base < total; base += stride) {
             const uint8_t *src[UNROLL];
             uint8_t *dst[UNROLL];
             bool zero[UNROLL];
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
-                const uint64_t item = base + u * kRowsPerStep + sub;
+                const uint32_t item = base + u * kRowsPerStep + sub;
                 src[u] = nullptr;
                 dst[u] = nullptr;
                 zero[u] = false;
                 if (item < total) {
-                    const uint32_t layer = uint32_t(item / p.rows);
-                    const uint32_t at = uint32_t(item - uint64_t(layer) * p.rows);
+                    const uint32_t layer = item / p.rows;
+                    const uint32_t at = item - layer * p.rows;
                     const int32_t x = __ldg(p.indices + item);
                     dst[u] = p.output + (uint64_t(layer) * p.capacity + at) * p.row_bytes;
                     if (x < 0) {
@@ -103,60 +300,70 @@ __global__ void __launch_bounds__(kGatherThreads, 2) gather_kernel(const __grid_
                         const uint32_t v = chunk + vlane + k * LPR;
                         if (dst[u] == nullptr || v >= vectors)
                             continue;
-                        if (zero[u])
-                            st_v4(dst[u] + uint64_t(v) * 16, Vec16{0, 0, 0, 0});
-                        else if (src[u] != nullptr)
-                            st_v4(dst[u] + uint64_t(v) * 16, buf[u][k]);
+                        st_v4(dst[u] + uint64_t(v) * 16, zero[u] ? Vec16{0, 0, 0, 0} : buf[u][k]);
                     }
             }
         }
     } else if (p.packs > 0) {
-        // Scale warps: one (layer, row) item per lane; for the column-major
-        // layout consecutive lanes take consecutive tokens of one entry slot so
-        // the strided output is written coalesced.
-        const uint32_t sf_lane = (warp - row_warps) * 32 + lane;
-        const uint64_t first = uint64_t(blockIdx.x) * p.sf_warps * 32 + sf_lane;
-        const uint64_t stride = uint64_t(gridDim.x) * p.sf_warps * 32;
-        for (uint64_t item = first; item < total; item += stride) {
-            const uint32_t layer = uint32_t(item / p.rows);
-            const uint32_t r = uint32_t(item - uint64_t(layer) * p.rows);
-            uint32_t token, slot;
-            if (p.col_major_sf) {
-                slot = r / p.tokens;
-                token = r - slot * p.tokens;
-            } else {
-                token = r / p.ept;
-                slot = r - token * p.ept;
-            }
-            const uint32_t at = token * p.ept + slot;
-            const int32_t x = __ldg(p.indices + uint64_t(layer) * p.rows + at);
-            float *out = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
-                         uint64_t(slot) * p.packs * p.sf_hidden_stride;
-            const float *src = nullptr;
-            if (x >= 0) {
-                const uint32_t span = s_entries[layer] * p.sf_shard_div;
-                const uint32_t shard = uint32_t(x) / span;
-                if (shard < p.world && s_sf[shard] != 0)
-                    src = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
-                          uint64_t(uint32_t(x) - shard * span) * p.packs;
-            }
-            for (uint32_t k = 0; k < p.packs; ++k)
-                out[uint64_t(k) * p.sf_hidden_stride] = src != nullptr ? __ldg(src + k) : 0.0f;
-        }
+        gather_scales(p, s_sf, s_entries, s_sfbase, blockIdx.x * p.sf_warps * 32 + (warp - row_warps) * 32 + lane,
+                      gridDim.x * p.sf_warps * 32);
     }
 }
 
 template <int LPR, int VPL, int UNROLL>
-cudaError_t launch_variant(const GatherParams &p, int num_sms, cudaStream_t stream) {
-    const uint32_t warps = kGatherThreads / 32;
-    const uint32_t row_warps = warps - p.sf_warps;
+cudaError_t launch_simt(GatherParams p, int num_sms, cudaStream_t stream) {
+    p.sf_warps = p.packs ? 2 : 0;
+    const uint32_t row_warps = kSimtThreads / 32 - p.sf_warps;
     const uint64_t total = uint64_t(p.layers) * p.rows;
     const uint64_t per_block = uint64_t(row_warps) * (32 / LPR) * UNROLL;
     uint64_t blocks = (total + per_block - 1) / per_block;
     blocks = blocks < uint64_t(num_sms) * 2 ? blocks : uint64_t(num_sms) * 2;
     if (blocks == 0)
         return cudaSuccess;
-    gather_kernel<LPR, VPL, UNROLL><<<unsigned(blocks), kGatherThreads, 0, stream>>>(p);
+    gather_simt_kernel<LPR, VPL, UNROLL><<<unsigned(blocks), kSimtThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t stream) {
+    const uint32_t vectors = p.row_bytes / 16;
+    if (vectors <= 4)
+        return launch_simt<4, 1, 4>(p, num_sms, stream);
+    if (vectors <= 8)
+        return launch_simt<8, 1, 4>(p, num_sms, stream);
+    if (vectors <= 16)
+        return launch_simt<16, 1, 4>(p, num_sms, stream);
+    if (vectors <= 32)
+        return launch_simt<32, 1, 4>(p, num_sms, stream);
+    if (vectors <= 64)
+        return launch_simt<32, 2, 2>(p, num_sms, stream);
+    return launch_simt<32, 4, 1>(p, num_sms, stream);
+}
+
+cudaError_t launch_bulk(const GatherParams &p, int num_sms, cudaStream_t stream) {
+    const uint32_t stage_bytes = kBulkTile * p.row_bytes;
+    uint32_t stages = kStageTargetBytes / stage_bytes;
+    stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
+    const size_t smem = size_t(stages) * stage_bytes + size_t(stages) * (16 + sizeof(StageMeta));
+    static size_t configured = 0;
+    if (smem > configured) {
+        cudaError_t rc =
+            cudaFuncSetAttribute(gather_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (rc != cudaSuccess)
+            return rc;
+        configured = smem;
+    }
+    int per_sm = 0;
+    cudaError_t rc = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gather_bulk_kernel, kBulkThreads, smem);
+    if (rc != cudaSuccess)
+        return rc;
+    per_sm = per_sm < 1 ? 1 : per_sm;
+    const uint32_t tiles_per_layer = (p.rows + kBulkTile - 1) / kBulkTile;
+    const uint32_t total_tiles = tiles_per_layer * p.layers;
+    uint32_t grid = uint32_t(num_sms) * uint32_t(per_sm);
+    grid = grid < total_tiles ? grid : total_tiles;
+    const uint32_t tiles_per_cta = (total_tiles + grid - 1) / grid;
+    grid = (total_tiles + tiles_per_cta - 1) / tiles_per_cta;
+    gather_bulk_kernel<<<grid, kBulkThreads, smem, stream>>>(p, tiles_per_layer, tiles_per_cta, stages);
     return cudaGetLastError();
 }
 
@@ -165,18 +372,10 @@ cudaError_t launch_variant(const GatherParams &p, int num_sms, cudaStream_t stre
 cudaError_t launch_gather(const GatherParams &p, int num_sms, cudaStream_t stream) {
     if (p.layers == 0 || p.rows == 0)
         return cudaSuccess;
-    const uint32_t vectors = p.row_bytes / 16;
-    if (vectors <= 4)
-        return launch_variant<4, 1, 4>(p, num_sms, stream);
-    if (vectors <= 8)
-        return launch_variant<8, 1, 4>(p, num_sms, stream);
-    if (vectors <= 16)
-        return launch_variant<16, 1, 4>(p, num_sms, stream);
-    if (vectors <= 32)
-        return launch_variant<32, 1, 4>(p, num_sms, stream);
-    if (vectors <= 64)
-        return launch_variant<32, 2, 2>(p, num_sms, stream);
-    return launch_variant<32, 4, 1>(p, num_sms, stream);
+    // The ring needs two stages of 32 rows; larger rows use the SIMT kernel.
+    if (p.variant == kGatherSimt || p.row_bytes > 2048)
+        return launch_simt_any(p, num_sms, stream);
+    return launch_bulk(p, num_sms, stream);
 }
 
 } // namespace engram

@@ -39,7 +39,11 @@ enum ErrorCode : uint32_t {
     kIndexOutOfRange = 2,  // a request named a row beyond the global vocabulary
     kInboxOverflow = 3,    // a request list exceeded the inbox slot
     kPushBounds = 4,       // an owner got a row id or position out of bounds
+    kPipelineTimeout = 5,  // a shared-memory pipeline barrier never completed
 };
+
+constexpr uint32_t kGatherBulk = 0;  // TMA bulk-copy ring (default)
+constexpr uint32_t kGatherSimt = 1;  // 16-byte vector loads
 
 
 // Mailbox header written by a requester's GPU into the owner's host shard and
@@ -78,6 +82,7 @@ struct GatherParams {
     uint32_t sf_token_stride, sf_hidden_stride, sf_layer_stride;
     uint32_t col_major_sf;
     uint32_t sf_warps;            // warps per CTA dedicated to scales (0 for BF16)
+    uint32_t variant;             // kGatherBulk or kGatherSimt
 };
 
 // Requester-side dispatch for host-route owners: append (row, position) pairs

@@ -79,6 +79,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         timeout_ns_ = uint64_t(get<double>(cfg, "timeout_s") * 1e9);
         token_ = get<std::string>(cfg, "token");
         allow_host_vmm_ = get<bool>(cfg, "allow_host_vmm");
+        gather_variant_ = get<std::string>(cfg, "gather_kernel") == "simt" ? kGatherSimt : kGatherBulk;
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
         capacity_ = max_tokens_ * ept_;
@@ -426,6 +427,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["fetches"] = fetches_;
         d["kernel_launches"] = launches_;
         d["num_sms"] = num_sms_;
+        d["gather_kernel"] = gather_variant_ == kGatherSimt ? "simt" : "tma_bulk";
         return d;
     }
 
@@ -592,6 +594,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.world = world_;
         g.packs = packs_;
         g.sf_warps = packs_ ? 2 : 0;
+        g.variant = gather_variant_;
 
         DispatchParams &d = dispatch_;
         d = DispatchParams{};
@@ -713,6 +716,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint32_t row_bytes_ = 0, capacity_ = 0;
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
+    uint32_t gather_variant_ = kGatherBulk;
     std::string token_;
     size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
            dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;
@@ -746,9 +750,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     std::string describe_error() const {
         volatile ErrorRecord *e = host_error_;
         static const char *names[] = {"ok", "hook wait timed out", "index outside the vocabulary",
-                                      "inbox overflow", "push bounds"};
+                                      "inbox overflow", "push bounds", "gather pipeline stalled"};
         const uint32_t s = e->status;
-        std::string what = s < 5 ? names[s] : "unknown error";
+        std::string what = s < 6 ? names[s] : "unknown error";
         return "Engram device error: " + what + " (layer " + std::to_string(e->layer) + ", owner " +
                std::to_string(e->owner) + ", observed " + std::to_string(e->observed) + ", expected " +
                std::to_string(e->expected) + ", reports " + std::to_string(e->count) + ")";

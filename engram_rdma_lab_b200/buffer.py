@@ -81,6 +81,14 @@ def theoretical_config(world, num_layers, num_max_tokens, num_entries_per_token,
     return channels, depth, False
 
 
+def _gather_kernel() -> str:
+    """``ENGRAM_GATHER_KERNEL``: ``bulk`` (TMA ring, default) or ``simt``."""
+    value = os.environ.get("ENGRAM_GATHER_KERNEL", "bulk")
+    if value not in ("bulk", "simt"):
+        raise ValueError("ENGRAM_GATHER_KERNEL must be 'bulk' or 'simt'")
+    return value
+
+
 class EngramBuffer(EngramBufferBase):
     """Native B200 EngramBuffer (peer-HBM and host-push routes)."""
 
@@ -186,6 +194,7 @@ class EngramBuffer(EngramBufferBase):
             channels=self.num_allocated_qps, egm=self.egm.enabled, local_sf=self.local_sf,
             timeout_s=self.num_gpu_timeout_secs, token=tokens[0],
             allow_host_vmm=env_flag("ENGRAM_HOST_VMM", True), plan=plan.as_native(),
+            gather_kernel=_gather_kernel(),
         )
         native = None
         with torch.cuda.device(self.device):
