@@ -32,6 +32,7 @@ constexpr int kBulkTile = 32;           // rows per stage: one producer lane per
 constexpr int kBulkThreads = 128;       // producer warp, consumer warp, 2 scale warps
 constexpr uint32_t kStageTargetBytes = 64 * 1024;
 constexpr uint64_t kPipelineTimeoutNs = 2000000000ull;
+constexpr uint32_t kIndexDepth = 8;     // tiles of indices in flight per producer
 
 struct StageMeta {
     uint32_t layer, start, count, direct_mask, zero_mask, pad[3];
@@ -107,6 +108,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
+    __shared__ int32_t s_index[kIndexDepth * kBulkTile];
     const uint32_t stage_bytes = kBulkTile * p.row_bytes;
     uint8_t *data = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(stages) * stage_bytes);
@@ -129,27 +131,34 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     const uint32_t t1 = min(t0 + tiles_per_cta, total_tiles);
 
     if (warp == 0) {
-        // Producer: classify the tile's rows and issue one bulk copy per direct row.
+        // Producer: classify the tile's rows and issue one bulk copy per direct
+        // row.  Indices arrive through a kIndexDepth-tile cp.async ring, so
+        // address generation never waits on a dependent global load.
         auto index_of = [&](uint32_t t, uint32_t &layer, uint32_t &start, uint32_t &count) {
             layer = t / tiles_per_layer;
             start = (t - layer * tiles_per_layer) * kBulkTile;
             count = min(uint32_t(kBulkTile), p.rows - start);
         };
-        uint32_t layer = 0, start = 0, count = 0;
-        int32_t x_next = -1;
-        if (t0 < t1) {
-            index_of(t0, layer, start, count);
-            x_next = lane < count ? __ldg(p.indices + layer * p.rows + start + lane) : -1;
-        }
+        auto prefetch = [&](uint32_t t, uint32_t slot) {
+            if (t < t1) {
+                uint32_t l, st, c;
+                index_of(t, l, st, c);
+                if (lane < c)
+                    cp_async_4(s_index + slot * kBulkTile + lane, p.indices + l * p.rows + st + lane);
+            }
+            cp_async_commit();  // one group per tile, empty past the end
+        };
+#pragma unroll
+        for (uint32_t d = 0; d < kIndexDepth; ++d)
+            prefetch(t0 + d, d);
         for (uint32_t t = t0, k = 0; t < t1; ++t, ++k) {
             const uint32_t stage = k % stages, phase = k / stages;
+            const uint32_t slot = k % kIndexDepth;
+            uint32_t layer, start, count;
             index_of(t, layer, start, count);
-            const int32_t x = x_next;
-            if (t + 1 < t1) {  // prefetch the next tile's indices
-                uint32_t nl, ns, nc;
-                index_of(t + 1, nl, ns, nc);
-                x_next = lane < nc ? __ldg(p.indices + nl * p.rows + ns + lane) : -1;
-            }
+            cp_async_wait<kIndexDepth - 1>();  // tile k's indices have landed
+            const int32_t x = lane < count ? s_index[slot * kBulkTile + lane] : -1;
+            prefetch(t + kIndexDepth, slot);
             if (k >= stages && !mbar_wait(empty + stage, (phase - 1) & 1, kPipelineTimeoutNs)) {
                 if (lane == 0)
                     report_error(p.error, kPipelineTimeout, layer, 0, t, 0);
@@ -183,6 +192,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
                 bulk_load(data + size_t(stage) * stage_bytes + size_t(lane) * p.row_bytes, src, p.row_bytes,
                           full + stage);
         }
+        cp_async_wait<0>();
     } else if (warp == 1) {
         // Consumer: stream each finished stage to the output.
         const uint32_t vectors = p.row_bytes / 16;
@@ -250,10 +260,23 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
         const uint32_t vectors = p.row_bytes / 16;
         const uint32_t first = (blockIdx.x * row_warps + warp) * kRowsPerIter;
         const uint32_t stride = gridDim.x * row_warps * kRowsPerIter;
+        int32_t xs[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const uint32_t item = first + u * kRowsPerStep + sub;
+            xs[u] = item < total ? __ldg(p.indices + item) : -1;
+        }
         for (uint32_t base = first; base < total; base += stride) {
             const uint8_t *src[UNROLL];
             uint8_t *dst[UNROLL];
             bool zero[UNROLL];
+            int32_t x_cur[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                x_cur[u] = xs[u];
+                const uint32_t next = base + stride + u * kRowsPerStep + sub;
+                xs[u] = next < total ? __ldg(p.indices + next) : -1;  // prefetch the next iteration
+            }
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
                 const uint32_t item = base + u * kRowsPerStep + sub;
@@ -263,7 +286,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                 if (item < total) {
                     const uint32_t layer = item / p.rows;
                     const uint32_t at = item - layer * p.rows;
-                    const int32_t x = __ldg(p.indices + item);
+                    const int32_t x = x_cur[u];
                     dst[u] = p.output + (uint64_t(layer) * p.capacity + at) * p.row_bytes;
                     if (x < 0) {
                         zero[u] = true;

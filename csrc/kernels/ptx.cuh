@@ -166,6 +166,17 @@ __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint3
                  : "memory");
 }
 
+// 4-byte asynchronous global -> shared copy (completes with cp.async.wait_group).
+__device__ __forceinline__ void cp_async_4(void *dst_smem, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ Vec16 ld_shared_v4(const void *p) {
     Vec16 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
