@@ -239,7 +239,7 @@ def main():
                 "route": args.route if native else "all_to_all",
                 "graph": bool(args.graph),
                 "distribution": spec.distribution,
-                "l2": "flushed between timed steps (256 MiB write outside the events); fresh indices per step",
+                "l2": "flushed between timed steps (256 MiB write + read-back outside the events); fresh indices per step",
                 "timing": "CUDA events per step on the launching stream, max over ranks",
                 "baseline_gbs_per_requester": BASELINE_GBS_PER_REQUESTER,
             },

@@ -242,124 +242,122 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 }
 
 // ------------------------------------------------------------ SIMT variant
-template <int LPR, int VPL, int UNROLL>
+// A warp owns groups of 32 consecutive (layer, row) items.  Lane l resolves
+// item l once (owner, source, destination, scales) and the copy loop hands the
+// 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
+// per-row integer work is done by one lane instead of LPR lanes.  The next
+// group's indices are loaded before this group's rows, hiding that latency.
+template <int LPR, int UNROLL>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
     load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
     __syncthreads();
 
-    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t row_warps = blockDim.x / 32 - p.sf_warps;
+    constexpr uint32_t kRowsPerStep = 32 / LPR;
+    const uint32_t lane = threadIdx.x % 32;
+    const uint32_t sub = lane / LPR, vlane = lane % LPR;
+    const uint32_t vectors = p.row_bytes / 16;
     const uint32_t total = p.layers * p.rows;
+    const uint32_t groups = (total + 31) / 32;
+    const uint32_t warp_id = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const uint32_t warp_stride = gridDim.x * (blockDim.x / 32);
 
-    if (warp < row_warps) {
-        constexpr uint32_t kRowsPerStep = 32 / LPR;
-        constexpr uint32_t kRowsPerIter = kRowsPerStep * UNROLL;
-        const uint32_t sub = lane / LPR, vlane = lane % LPR;
-        const uint32_t vectors = p.row_bytes / 16;
-        const uint32_t first = (blockIdx.x * row_warps + warp) * kRowsPerIter;
-        const uint32_t stride = gridDim.x * row_warps * kRowsPerIter;
-        int32_t xs[UNROLL];
-#pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const uint32_t item = first + u * kRowsPerStep + sub;
-            xs[u] = item < total ? __ldg(p.indices + item) : -1;
+    int32_t x_next = -1;
+    if (warp_id < groups) {
+        const uint32_t item = warp_id * 32 + lane;
+        x_next = item < total ? __ldg(p.indices + item) : -1;
+    }
+    for (uint32_t g = warp_id; g < groups; g += warp_stride) {
+        const uint32_t item = g * 32 + lane;
+        const int32_t x = x_next;
+        const uint32_t g_next = g + warp_stride;
+        if (g_next < groups) {
+            const uint32_t nitem = g_next * 32 + lane;
+            x_next = nitem < total ? __ldg(p.indices + nitem) : -1;
         }
-        for (uint32_t base = first; base < total; base += stride) {
-            const uint8_t *src[UNROLL];
-            uint8_t *dst[UNROLL];
-            bool zero[UNROLL];
-            int32_t x_cur[UNROLL];
-#pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
-                x_cur[u] = xs[u];
-                const uint32_t next = base + stride + u * kRowsPerStep + sub;
-                xs[u] = next < total ? __ldg(p.indices + next) : -1;  // prefetch the next iteration
-            }
-#pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
-                const uint32_t item = base + u * kRowsPerStep + sub;
-                src[u] = nullptr;
-                dst[u] = nullptr;
-                zero[u] = false;
-                if (item < total) {
-                    const uint32_t layer = item / p.rows;
-                    const uint32_t at = item - layer * p.rows;
-                    const int32_t x = x_cur[u];
-                    dst[u] = p.output + (uint64_t(layer) * p.capacity + at) * p.row_bytes;
-                    if (x < 0) {
-                        zero[u] = true;
-                    } else {
-                        const uint32_t n = s_entries[layer];
-                        const uint32_t owner = uint32_t(x) / n;
-                        if (owner >= p.world) {
-                            zero[u] = true;
-                            if (vlane == 0)
-                                report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
-                        } else if (s_direct[owner] != 0) {
-                            const uint64_t row = uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n);
-                            src[u] = reinterpret_cast<const uint8_t *>(s_direct[owner]) + row * p.row_bytes;
-                        } else {
-                            dst[u] = nullptr;  // host route: the owner pushes this row
-                        }
-                    }
+        // Resolve this lane's item.
+        uint64_t src = 0, dst = 0;  // src == 0 && dst != 0: zero row; dst == 0: not ours
+        if (item < total) {
+            const uint32_t layer = item / p.rows;
+            const uint32_t at = item - layer * p.rows;
+            dst = reinterpret_cast<uint64_t>(p.output) + (uint64_t(layer) * p.capacity + at) * p.row_bytes;
+            if (x >= 0) {
+                const uint32_t n = s_entries[layer];
+                const uint32_t owner = uint32_t(x) / n;
+                if (owner >= p.world) {
+                    report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
+                } else if (s_direct[owner] != 0) {
+                    src = s_direct[owner] + (uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n)) * p.row_bytes;
+                } else {
+                    dst = 0;  // host route: the owner pushes this row
                 }
             }
-            for (uint32_t chunk = 0; chunk < vectors; chunk += LPR * VPL) {
-                Vec16 buf[UNROLL][VPL];
-#pragma unroll
-                for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-                    for (int k = 0; k < VPL; ++k) {
-                        const uint32_t v = chunk + vlane + k * LPR;
-                        if (src[u] != nullptr && v < vectors)
-                            buf[u][k] = ld_nc_na_v4(src[u] + uint64_t(v) * 16);
-                    }
-#pragma unroll
-                for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-                    for (int k = 0; k < VPL; ++k) {
-                        const uint32_t v = chunk + vlane + k * LPR;
-                        if (dst[u] == nullptr || v >= vectors)
-                            continue;
-                        st_v4(dst[u] + uint64_t(v) * 16, zero[u] ? Vec16{0, 0, 0, 0} : buf[u][k]);
-                    }
+            if (p.packs > 0) {
+                const uint32_t token = at / p.ept, slot = at - token * p.ept;
+                float *out = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
+                             uint64_t(slot) * p.packs * p.sf_hidden_stride;
+                const float *sf = nullptr;
+                if (x >= 0) {
+                    const uint32_t span = s_entries[layer] * p.sf_shard_div;
+                    const uint32_t shard = uint32_t(x) / span;
+                    if (shard < p.world && s_sf[shard] != 0)
+                        sf = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
+                             uint64_t(uint32_t(x) - shard * span) * p.packs;
+                }
+                for (uint32_t k = 0; k < p.packs; ++k)
+                    out[uint64_t(k) * p.sf_hidden_stride] = sf != nullptr ? __ldg(sf + k) : 0.0f;
             }
         }
-    } else if (p.packs > 0) {
-        gather_scales(p, s_sf, s_entries, s_sfbase, blockIdx.x * p.sf_warps * 32 + (warp - row_warps) * 32 + lane,
-                      gridDim.x * p.sf_warps * 32);
+        // Copy the group's rows, UNROLL row-steps of loads in flight per lane.
+        for (uint32_t r0 = 0; r0 < 32; r0 += kRowsPerStep * UNROLL) {
+            uint64_t rs[UNROLL], rd[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                const uint32_t r = r0 + u * kRowsPerStep + sub;
+                rs[u] = __shfl_sync(0xFFFFFFFFu, src, r);
+                rd[u] = __shfl_sync(0xFFFFFFFFu, dst, r);
+            }
+            for (uint32_t v = vlane; v < vectors; v += LPR) {
+                Vec16 buf[UNROLL];
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) {
+                    buf[u] = Vec16{0, 0, 0, 0};
+                    if (rs[u] != 0)
+                        buf[u] = ld_nc_na_v4(reinterpret_cast<const uint8_t *>(rs[u]) + uint64_t(v) * 16);
+                }
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u)
+                    if (rd[u] != 0)
+                        st_v4(reinterpret_cast<uint8_t *>(rd[u]) + uint64_t(v) * 16, buf[u]);
+            }
+        }
     }
 }
 
-template <int LPR, int VPL, int UNROLL>
-cudaError_t launch_simt(GatherParams p, int num_sms, cudaStream_t stream) {
-    p.sf_warps = p.packs ? 2 : 0;
-    const uint32_t row_warps = kSimtThreads / 32 - p.sf_warps;
-    const uint64_t total = uint64_t(p.layers) * p.rows;
-    const uint64_t per_block = uint64_t(row_warps) * (32 / LPR) * UNROLL;
-    uint64_t blocks = (total + per_block - 1) / per_block;
-    blocks = blocks < uint64_t(num_sms) * 2 ? blocks : uint64_t(num_sms) * 2;
+template <int LPR, int UNROLL>
+cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream) {
+    const uint32_t total = p.layers * p.rows;
+    const uint32_t groups = (total + 31) / 32;
+    const uint32_t warps = kSimtThreads / 32;
+    uint32_t blocks = (groups + warps - 1) / warps;
+    const uint32_t cap = uint32_t(num_sms) * 2;
+    blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
         return cudaSuccess;
-    gather_simt_kernel<LPR, VPL, UNROLL><<<unsigned(blocks), kSimtThreads, 0, stream>>>(p);
+    gather_simt_kernel<LPR, UNROLL><<<blocks, kSimtThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t vectors = p.row_bytes / 16;
     if (vectors <= 4)
-        return launch_simt<4, 1, 4>(p, num_sms, stream);
+        return launch_simt<4, 4>(p, num_sms, stream);
     if (vectors <= 8)
-        return launch_simt<8, 1, 4>(p, num_sms, stream);
+        return launch_simt<8, 4>(p, num_sms, stream);
     if (vectors <= 16)
-        return launch_simt<16, 1, 4>(p, num_sms, stream);
-    if (vectors <= 32)
-        return launch_simt<32, 1, 4>(p, num_sms, stream);
-    if (vectors <= 64)
-        return launch_simt<32, 2, 2>(p, num_sms, stream);
-    return launch_simt<32, 4, 1>(p, num_sms, stream);
+        return launch_simt<16, 4>(p, num_sms, stream);
+    return launch_simt<32, 4>(p, num_sms, stream);
 }
 
 cudaError_t launch_bulk(const GatherParams &p, int num_sms, cudaStream_t stream) {

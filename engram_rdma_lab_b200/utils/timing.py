@@ -21,13 +21,23 @@ L2_FLUSH_BYTES = 256 << 20
 
 
 class L2Flusher:
+    """Evict the L2 between timed steps.
+
+    Writes a buffer twice the L2 size, then reads it back: the write evicts
+    every line the previous step left behind, and the read makes the flush's
+    own dirty lines drain to DRAM here, outside the timed region, instead of
+    during the next step.
+    """
+
     def __init__(self, nbytes: int = L2_FLUSH_BYTES, device=None):
         self.buffer = torch.empty(nbytes // 4, dtype=torch.int32, device=device or "cuda")
+        self.sink = torch.empty((), dtype=torch.int64, device=device or "cuda")
         self._value = 0
 
     def __call__(self):
         self._value ^= 1
         self.buffer.fill_(self._value)
+        torch.sum(self.buffer, dtype=torch.int64, out=self.sink)
 
 
 def event_ms(fn, stream=None) -> float:
