@@ -37,7 +37,7 @@ class L2Flusher:
     def __call__(self):
         self._value ^= 1
         self.buffer.fill_(self._value)
-        torch.sum(self.buffer, dtype=torch.int64, out=self.sink)
+        torch.sum(self.buffer, dim=0, dtype=torch.int64, out=self.sink)
 
 
 def event_ms(fn, stream=None) -> float:

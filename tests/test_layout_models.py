@@ -145,3 +145,15 @@ def test_fp8_roundtrip():
     assert rel < 0.07  # e4m3 has a 3-bit mantissa
     codes2, scales2 = quantize_fp8_blockwise(x, power_of_two=True)
     assert torch.all(torch.log2(scales2) == torch.round(torch.log2(scales2)))
+
+
+def test_l2_flusher_and_percentile_on_cpu():
+    from engram_rdma_lab_b200.utils.timing import L2Flusher, percentile
+
+    f = L2Flusher(nbytes=4096, device="cpu")
+    f()
+    assert int(f.sink) == 1024 and int(f.buffer[0]) == 1
+    f()
+    assert int(f.sink) == 0
+    assert percentile([1.0, 2.0, 3.0, 4.0], 0.5) == 2.5
+    assert percentile([5.0], 0.99) == 5.0
