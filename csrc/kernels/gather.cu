@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 // 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
 // per-row integer work is done by one lane instead of LPR lanes.  The next
 // group's indices are loaded before this group's rows, hiding that latency.
-template <int LPR, int UNROLL>
+template <int LPR, int VPL, int UNROLL>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     __syncthreads();
 
     constexpr uint32_t kRowsPerStep = 32 / LPR;
+    constexpr uint32_t kMaxPacksInFlight = 4;
     const uint32_t lane = threadIdx.x % 32;
     const uint32_t sub = lane / LPR, vlane = lane % LPR;
     const uint32_t vectors = p.row_bytes / 16;
@@ -276,8 +277,12 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
             const uint32_t nitem = g_next * 32 + lane;
             x_next = nitem < total ? __ldg(p.indices + nitem) : -1;
         }
-        // Resolve this lane's item.
+        // Resolve this lane's item; its scale loads are issued now and stored
+        // after the rows, so their latency overlaps the row copies.
         uint64_t src = 0, dst = 0;  // src == 0 && dst != 0: zero row; dst == 0: not ours
+        float *sf_out = nullptr;
+        const float *sf_src = nullptr;
+        float sf_val[kMaxPacksInFlight];
         if (item < total) {
             const uint32_t layer = item / p.rows;
             const uint32_t at = item - layer * p.rows;
@@ -295,21 +300,21 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
             }
             if (p.packs > 0) {
                 const uint32_t token = at / p.ept, slot = at - token * p.ept;
-                float *out = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
-                             uint64_t(slot) * p.packs * p.sf_hidden_stride;
-                const float *sf = nullptr;
+                sf_out = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
+                         uint64_t(slot) * p.packs * p.sf_hidden_stride;
                 if (x >= 0) {
                     const uint32_t span = s_entries[layer] * p.sf_shard_div;
                     const uint32_t shard = uint32_t(x) / span;
                     if (shard < p.world && s_sf[shard] != 0)
-                        sf = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
-                             uint64_t(uint32_t(x) - shard * span) * p.packs;
+                        sf_src = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
+                                 uint64_t(uint32_t(x) - shard * span) * p.packs;
                 }
-                for (uint32_t k = 0; k < p.packs; ++k)
-                    out[uint64_t(k) * p.sf_hidden_stride] = sf != nullptr ? __ldg(sf + k) : 0.0f;
+#pragma unroll
+                for (uint32_t k = 0; k < kMaxPacksInFlight; ++k)
+                    sf_val[k] = (sf_src != nullptr && k < p.packs) ? __ldg(sf_src + k) : 0.0f;
             }
         }
-        // Copy the group's rows, UNROLL row-steps of loads in flight per lane.
+        // Copy the group's rows: UNROLL row-steps x VPL vectors in flight per lane.
         for (uint32_t r0 = 0; r0 < 32; r0 += kRowsPerStep * UNROLL) {
             uint64_t rs[UNROLL], rd[UNROLL];
 #pragma unroll
@@ -318,24 +323,39 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                 rs[u] = __shfl_sync(0xFFFFFFFFu, src, r);
                 rd[u] = __shfl_sync(0xFFFFFFFFu, dst, r);
             }
-            for (uint32_t v = vlane; v < vectors; v += LPR) {
-                Vec16 buf[UNROLL];
-#pragma unroll
-                for (int u = 0; u < UNROLL; ++u) {
-                    buf[u] = Vec16{0, 0, 0, 0};
-                    if (rs[u] != 0)
-                        buf[u] = ld_nc_na_v4(reinterpret_cast<const uint8_t *>(rs[u]) + uint64_t(v) * 16);
-                }
+            for (uint32_t chunk = 0; chunk < vectors; chunk += LPR * VPL) {
+                Vec16 buf[UNROLL][VPL];
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
-                    if (rd[u] != 0)
-                        st_v4(reinterpret_cast<uint8_t *>(rd[u]) + uint64_t(v) * 16, buf[u]);
+#pragma unroll
+                    for (int k = 0; k < VPL; ++k) {
+                        const uint32_t v = chunk + vlane + k * LPR;
+                        buf[u][k] = Vec16{0, 0, 0, 0};
+                        if (rs[u] != 0 && v < vectors)
+                            buf[u][k] = ld_nc_na_v4(reinterpret_cast<const uint8_t *>(rs[u]) + uint64_t(v) * 16);
+                    }
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+                    for (int k = 0; k < VPL; ++k) {
+                        const uint32_t v = chunk + vlane + k * LPR;
+                        if (rd[u] != 0 && v < vectors)
+                            st_v4(reinterpret_cast<uint8_t *>(rd[u]) + uint64_t(v) * 16, buf[u][k]);
+                    }
             }
+        }
+        if (sf_out != nullptr) {
+#pragma unroll
+            for (uint32_t k = 0; k < kMaxPacksInFlight; ++k)
+                if (k < p.packs)
+                    sf_out[uint64_t(k) * p.sf_hidden_stride] = sf_val[k];
+            for (uint32_t k = kMaxPacksInFlight; k < p.packs; ++k)
+                sf_out[uint64_t(k) * p.sf_hidden_stride] = sf_src != nullptr ? __ldg(sf_src + k) : 0.0f;
         }
     }
 }
 
-template <int LPR, int UNROLL>
+template <int LPR, int VPL, int UNROLL>
 cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t total = p.layers * p.rows;
     const uint32_t groups = (total + 31) / 32;
@@ -345,19 +365,23 @@ cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream)
     blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
         return cudaSuccess;
-    gather_simt_kernel<LPR, UNROLL><<<blocks, kSimtThreads, 0, stream>>>(p);
+    gather_simt_kernel<LPR, VPL, UNROLL><<<blocks, kSimtThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t vectors = p.row_bytes / 16;
+    if (vectors <= 2)
+        return launch_simt<2, 1, 4>(p, num_sms, stream);
     if (vectors <= 4)
-        return launch_simt<4, 4>(p, num_sms, stream);
+        return launch_simt<4, 1, 4>(p, num_sms, stream);
     if (vectors <= 8)
-        return launch_simt<8, 4>(p, num_sms, stream);
+        return launch_simt<4, 2, 4>(p, num_sms, stream);
     if (vectors <= 16)
-        return launch_simt<16, 4>(p, num_sms, stream);
-    return launch_simt<32, 4>(p, num_sms, stream);
+        return launch_simt<8, 2, 4>(p, num_sms, stream);
+    if (vectors <= 32)
+        return launch_simt<16, 2, 4>(p, num_sms, stream);
+    return launch_simt<32, 2, 4>(p, num_sms, stream);
 }
 
 cudaError_t launch_bulk(const GatherParams &p, int num_sms, cudaStream_t stream) {

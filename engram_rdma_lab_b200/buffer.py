@@ -82,8 +82,8 @@ def theoretical_config(world, num_layers, num_max_tokens, num_entries_per_token,
 
 
 def _gather_kernel() -> str:
-    """``ENGRAM_GATHER_KERNEL``: ``bulk`` (TMA ring, default) or ``simt``."""
-    value = os.environ.get("ENGRAM_GATHER_KERNEL", "bulk")
+    """``ENGRAM_GATHER_KERNEL``: ``simt`` (16-byte vector loads, default) or ``bulk`` (TMA ring)."""
+    value = os.environ.get("ENGRAM_GATHER_KERNEL", "simt")
     if value not in ("bulk", "simt"):
         raise ValueError("ENGRAM_GATHER_KERNEL must be 'bulk' or 'simt'")
     return value
