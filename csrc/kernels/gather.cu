@@ -361,7 +361,7 @@ cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream)
     const uint32_t groups = (total + 31) / 32;
     const uint32_t warps = kSimtThreads / 32;
     uint32_t blocks = (groups + warps - 1) / warps;
-    const uint32_t cap = uint32_t(num_sms) * 2;
+    const uint32_t cap = uint32_t(num_sms) * (p.ctas_per_sm ? p.ctas_per_sm : 2);
     blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
         return cudaSuccess;
@@ -377,8 +377,15 @@ cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t str
         return launch_simt<4, 1, 4>(p, num_sms, stream);
     if (vectors <= 8)
         return launch_simt<4, 2, 4>(p, num_sms, stream);
-    if (vectors <= 16)
+    if (vectors <= 16) {
+        if (p.unroll == 2)
+            return launch_simt<8, 2, 2>(p, num_sms, stream);
+        if (p.unroll == 8)
+            return launch_simt<8, 2, 8>(p, num_sms, stream);
+        if (p.unroll == 1)
+            return launch_simt<16, 1, 4>(p, num_sms, stream);
         return launch_simt<8, 2, 4>(p, num_sms, stream);
+    }
     if (vectors <= 32)
         return launch_simt<16, 2, 4>(p, num_sms, stream);
     return launch_simt<32, 2, 4>(p, num_sms, stream);

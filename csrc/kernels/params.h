@@ -83,6 +83,8 @@ struct GatherParams {
     uint32_t col_major_sf;
     uint32_t sf_warps;            // warps per CTA dedicated to scales (0 for BF16)
     uint32_t variant;             // kGatherBulk or kGatherSimt
+    uint32_t ctas_per_sm;         // SIMT grid cap per SM (0 = default 2)
+    uint32_t unroll;              // SIMT row-steps in flight for 256-byte rows (0 = default)
 };
 
 // Requester-side dispatch for host-route owners: append (row, position) pairs

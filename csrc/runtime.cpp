@@ -80,6 +80,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         token_ = get<std::string>(cfg, "token");
         allow_host_vmm_ = get<bool>(cfg, "allow_host_vmm");
         gather_variant_ = get<std::string>(cfg, "gather_kernel") == "simt" ? kGatherSimt : kGatherBulk;
+        tuning_ctas_per_sm_ = get<uint32_t>(cfg, "gather_ctas_per_sm");
+        tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
         capacity_ = max_tokens_ * ept_;
@@ -595,6 +597,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.packs = packs_;
         g.sf_warps = packs_ ? 2 : 0;
         g.variant = gather_variant_;
+        g.ctas_per_sm = tuning_ctas_per_sm_;
+        g.unroll = tuning_unroll_;
 
         DispatchParams &d = dispatch_;
         d = DispatchParams{};
@@ -716,7 +720,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint32_t row_bytes_ = 0, capacity_ = 0;
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
-    uint32_t gather_variant_ = kGatherBulk;
+    uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0;
     std::string token_;
     size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
            dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;

@@ -195,6 +195,8 @@ class EngramBuffer(EngramBufferBase):
             timeout_s=self.num_gpu_timeout_secs, token=tokens[0],
             allow_host_vmm=env_flag("ENGRAM_HOST_VMM", True), plan=plan.as_native(),
             gather_kernel=_gather_kernel(),
+            gather_ctas_per_sm=env_int("ENGRAM_GATHER_CTAS_PER_SM", 0, minimum=0),
+            gather_unroll=env_int("ENGRAM_GATHER_UNROLL", 0, minimum=0),
         )
         native = None
         with torch.cuda.device(self.device):
