@@ -190,7 +190,30 @@ __global__ void wait_probe_kernel(const uint64_t *flag, uint64_t expected, uint6
         report_error(error, kWaitTimeout, 0, 0, seen, expected);
 }
 
+// Streaming 16-byte copy used to measure the peer-memory envelope (pull: the
+// source is a peer mapping; push: the destination is).
+__global__ void __launch_bounds__(512) stream_copy_kernel(const Vec16 *src, Vec16 *dst, uint64_t vectors) {
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < vectors; i += 4 * stride) {
+        Vec16 a = ld_nc_na_v4(src + i), b = ld_nc_na_v4(src + i + stride), c = ld_nc_na_v4(src + i + 2 * stride),
+              d = ld_nc_na_v4(src + i + 3 * stride);
+        st_v4(dst + i, a);
+        st_v4(dst + i + stride, b);
+        st_v4(dst + i + 2 * stride, c);
+        st_v4(dst + i + 3 * stride, d);
+    }
+    for (; i < vectors; i += stride)
+        st_v4(dst + i, ld_nc_na_v4(src + i));
+}
+
 } // namespace
+
+cudaError_t launch_stream_copy(const void *src, void *dst, uint64_t bytes, int blocks, cudaStream_t stream) {
+    stream_copy_kernel<<<blocks, 512, 0, stream>>>(static_cast<const Vec16 *>(src), static_cast<Vec16 *>(dst),
+                                                   bytes / 16);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream) {
     if (p.rows == 0 || p.layers == 0)

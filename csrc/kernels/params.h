@@ -141,6 +141,8 @@ cudaError_t launch_gather(const GatherParams &p, int num_sms, cudaStream_t strea
 cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream);
 cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream);
 cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream);
+// 16-byte streaming copy (peer-bandwidth diagnostics).
+cudaError_t launch_stream_copy(const void *src, void *dst, uint64_t bytes, int blocks, cudaStream_t stream);
 // Bounded wait on a flag nothing sets; used by the timeout self-test.
 cudaError_t launch_wait_probe(const uint64_t *flag, uint64_t expected, uint64_t timeout_ns, ErrorSink error,
                               cudaStream_t stream);

@@ -495,6 +495,34 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         return d;
     }
 
+    // Peer bandwidth diagnostic: copy `bytes` between this GPU's output region
+    // and peer `peer`'s (push = store into the peer, else load from it).
+    // Returns the device time in microseconds.  Not for use during fetches.
+    double debug_peer_copy(uint32_t peer, size_t bytes, bool push, int blocks) {
+        check(connected_ && peer < world_ && (peer == rank_ || peer_dev_[peer]), "peer not mapped");
+        const size_t region = size_t(layers_) * capacity_ * row_bytes_;
+        bytes = std::min(bytes, region) / 16 * 16;
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        void *mine = reinterpret_cast<void *>(arena_->ptr() + dev_output_);
+        void *theirs = reinterpret_cast<void *>((peer == rank_ ? arena_->ptr() : peer_dev_[peer]->ptr()) +
+                                                dev_output_);
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, s);
+        check_cuda(push ? launch_stream_copy(mine, theirs, bytes, blocks, s)
+                        : launch_stream_copy(theirs, mine, bytes, blocks, s),
+                   "peer copy");
+        cudaEventRecord(b, s);
+        check_cuda(cudaEventSynchronize(b), "peer copy sync");
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        return double(ms) * 1e3;
+    }
+
     // Fault injection for tests: stop serving requesters, as a dead owner
     // process would.  Requesters then see their bounded hook wait run out.
     void debug_stop_service() {
@@ -866,6 +894,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("debug_state", &Runtime::debug_state)
         .def("run_wait_probe", &Runtime::run_wait_probe)
         .def("debug_stop_service", &Runtime::debug_stop_service)
+        .def("debug_peer_copy", &Runtime::debug_peer_copy)
         .def("close", &Runtime::close)
         .def_property_readonly("closed", &Runtime::closed);
     py::class_<OwnerServiceHarness>(m, "OwnerServiceHarness")
