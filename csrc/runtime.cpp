@@ -79,7 +79,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         timeout_ns_ = uint64_t(get<double>(cfg, "timeout_s") * 1e9);
         token_ = get<std::string>(cfg, "token");
         allow_host_vmm_ = get<bool>(cfg, "allow_host_vmm");
-        gather_variant_ = get<std::string>(cfg, "gather_kernel") == "simt" ? kGatherSimt : kGatherBulk;
+        gather_choice_ = get<std::string>(cfg, "gather_kernel");
+        gather_variant_ = gather_choice_ == "bulk" ? kGatherBulk : kGatherSimt;
         tuning_ctas_per_sm_ = get<uint32_t>(cfg, "gather_ctas_per_sm");
         tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
         layers_ = uint32_t(entries_.size());
@@ -231,6 +232,14 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 serves_any_ = true;
                 serve_[p] = 1;
             }
+        if (gather_choice_ == "auto") {
+            // Remote rows favour the TMA ring (deep asynchronous queue over
+            // NVLink); purely local gathers favour 16-byte vector loads.
+            bool remote_direct = false;
+            for (uint32_t p = 0; p < world_; ++p)
+                remote_direct |= (p != rank_ && routes_[p] == kPeerHbm);
+            gather_variant_ = remote_direct ? kGatherBulk : kGatherSimt;
+        }
         build_params();
         // Every peer imported our descriptors during its probe, which finished
         // before the probe reports were exchanged.
@@ -749,6 +758,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
     uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0;
+    std::string gather_choice_ = "auto";
     std::string token_;
     size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
            dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;

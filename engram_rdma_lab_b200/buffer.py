@@ -82,10 +82,16 @@ def theoretical_config(world, num_layers, num_max_tokens, num_entries_per_token,
 
 
 def _gather_kernel() -> str:
-    """``ENGRAM_GATHER_KERNEL``: ``simt`` (16-byte vector loads, default) or ``bulk`` (TMA ring)."""
-    value = os.environ.get("ENGRAM_GATHER_KERNEL", "simt")
-    if value not in ("bulk", "simt"):
-        raise ValueError("ENGRAM_GATHER_KERNEL must be 'bulk' or 'simt'")
+    """``ENGRAM_GATHER_KERNEL``: ``auto`` (default), ``simt`` or ``bulk``.
+
+    ``simt`` moves rows with 16-byte vector loads and is fastest when every row
+    is local (HBM gather); ``bulk`` moves each row with a TMA bulk copy into a
+    shared-memory ring and is fastest when rows come from peers over NVLink.
+    ``auto`` picks ``bulk`` when any remote owner is on the peer-HBM route.
+    """
+    value = os.environ.get("ENGRAM_GATHER_KERNEL", "auto")
+    if value not in ("auto", "bulk", "simt"):
+        raise ValueError("ENGRAM_GATHER_KERNEL must be 'auto', 'bulk' or 'simt'")
     return value
 
 
