@@ -1,0 +1,49 @@
+"""Single-GPU ops: per-owner request packing vs. a plain torch reference."""
+
+import pytest
+import torch
+
+from engram_rdma_lab_b200.models import make_indices
+from engram_rdma_lab_b200.ops import route_pack, route_pack_reference
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    torch.cuda.set_device(0)
+
+
+def canonical(packed, counts, world, layers):
+    out = {}
+    for o in range(world):
+        for layer in range(layers):
+            n = int(counts[layer, o])
+            out[(o, layer)] = torch.sort(packed[o, layer, :n].cpu()).values
+    return out
+
+
+@pytest.mark.parametrize("world,tokens,ept", [(8, 4096, 24), (3, 1000, 7), (64, 33, 5), (1, 5, 1)])
+def test_route_pack_matches_reference(world, tokens, ept):
+    entries = (1031, 997)
+    idx = make_indices(0, world, entries, tokens, ept, padding=0.05, device="cuda")
+    owners = [1 if o % 3 != 1 else 0 for o in range(world)]
+    packed, counts = route_pack(idx, entries, world, owners)
+    torch.cuda.synchronize()
+    ref, ref_counts = route_pack_reference(idx, entries, world, owners)
+    assert torch.equal(counts.cpu(), ref_counts)
+    got = canonical(packed, counts, world, len(entries))
+    for key, want in ref.items():
+        assert torch.equal(got[key], torch.sort(want).values), key
+
+
+def test_route_pack_empty_and_padding_only():
+    entries = (100,)
+    idx = torch.full((1, 16, 4), -1, dtype=torch.int32, device="cuda")
+    packed, counts = route_pack(idx, entries, 4)
+    assert int(counts.sum()) == 0
+    empty = torch.empty(1, 0, 4, dtype=torch.int32, device="cuda")
+    packed, counts = route_pack(empty, entries, 4)
+    assert int(counts.sum()) == 0
