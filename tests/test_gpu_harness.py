@@ -1,0 +1,45 @@
+"""Drive benchmarks/test_engram.py through torchrun on two GPUs (scenario coverage)."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from .conftest import cuda_device_count, free_port
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(cuda_device_count() < 2, reason="needs two GPUs")]
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SMALL = ["--entries", "4099,4111", "--hidden", "128", "--ept", "7", "--tokens", "512", "--rounds", "4",
+         "--warmups", "1"]
+
+SCENARIOS = {
+    "graph_reverse_cross_stream": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--cuda-graph", "--hook-order",
+                                           "reverse", "--cross-stream", "--padding", "0.1"],
+    "locality_cycle_async": SMALL + ["--dtype", "bf16", "--locality-cycle", "--async-check", "--rounds", "12"],
+    "host_route_misc": SMALL + ["--dtype", "bf16", "--route", "host", "--vary-tokens", "--check-errors",
+                                "--rewrite", "--cpu-write", "--row-major-sf"],
+    "host_route_graph_locality": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--route", "host", "--cuda-graph",
+                                          "--locality-cycle", "--async-check", "--rounds", "12"],
+    "probe_fault_fallback": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--egm-fail-pair", "0:1"],
+    "single_owner_traffic": SMALL + ["--dtype", "bf16", "--traffic", "single", "--requester-rank", "0",
+                                     "--owner-rank", "1", "--distribution", "matched"],
+    "torch_baseline": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--impl", "torch", "--padding", "0.05"],
+}
+
+
+@pytest.mark.parametrize("name", sorted(SCENARIOS))
+def test_harness_scenario(name, tmp_path):
+    out = tmp_path / name
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(ROOT, "benchmarks", "test_engram.py"), *SCENARIOS[name], "--output-dir", str(out)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    meta = json.loads((out / "engram-r0.json").read_text())["metadata"]
+    if name == "probe_fault_fallback":
+        assert meta["routing"]["owner_routes"] == ["peer_hbm", "host"]
+        assert "0->1" in meta["routing"]["owner_fallback_reasons"][1]
