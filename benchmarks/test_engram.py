@@ -206,7 +206,7 @@ def main():
         T = indices.shape[1]
         for layer, out in enumerate(outputs):
             data, sf = out if packs else (out, None)
-            got = data.view(torch.uint8).reshape(T, -1)
+            got = data.view(torch.uint8).reshape(T, args.ept * args.hidden * dtype.itemsize)
             bad = bad + (got if on_gpu else got.cpu()).ne(exp[layer][0]).sum()
             if packs:
                 want = (args.ept * packs, 1) if args.row_major_sf else (1, (T + 3) // 4 * 4)

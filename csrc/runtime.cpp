@@ -654,7 +654,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d.capacity = capacity_;
         d.world = world_;
         d.rank = rank_;
-        d.tile_rows = 4096;
+        d.tile_rows = 512;
 
         PushParams &p = push_template_;
         p = PushParams{};
@@ -917,7 +917,7 @@ void route_pack(const torch::Tensor &indices, const std::vector<uint32_t> &entri
     d.world = world;
     d.rank = 0;
     d.channels = 1;
-    d.tile_rows = 4096;
+    d.tile_rows = 512;
     check_cuda(cudaMemsetAsync(d.cursors, 0, (lw + layers) * 4, s), "clear pack scratch");
     if (rows == 0) {
         check_cuda(cudaMemsetAsync(d.totals, 0, lw * 4, s), "clear counts");
