@@ -84,6 +84,7 @@ def parse():
     p.add_argument("--profile", action="store_true")
     p.add_argument("--profile-rank", type=int, default=0)
     p.add_argument("--egm-fail-pair", type=parse_pair, action="append", default=[])
+    p.add_argument("--timeout", type=float, default=60.0, help="bounded GPU wait per hook, seconds")
     p.add_argument("--output-dir", required=True)
     a = p.parse_args()
     if a.tokens < 0 or a.rounds < 1 or (a.capacity and a.capacity < max(1, a.tokens)):
@@ -142,7 +143,8 @@ def main():
     group = dist.group.WORLD
     sizes = cls.get_storage_size_hint(group, entries, args.hidden, capacity, args.ept, dtype, packs)
     qps, depth, restrict = cls.get_theoretical_config(group, len(entries), capacity, args.ept)
-    buffer = cls(group, *sizes, True, qps, depth, restrict, num_gpu_timeout_secs=60, explicitly_destroy=True)
+    buffer = cls(group, *sizes, True, qps, depth, restrict, num_gpu_timeout_secs=args.timeout,
+                 explicitly_destroy=True)
     buffer.set_config(entries, args.hidden, capacity, args.ept, dtype, packs)
 
     def load_weights(salt):
@@ -152,8 +154,19 @@ def main():
             scales = [s.cpu() for s in scales] if scales else None
         buffer.write(storages, scales)
 
+    t_phase = time.perf_counter()
+
+    def mark(name):
+        nonlocal t_phase
+        now = time.perf_counter()
+        meta.setdefault("phase_s", {})[name] = round(now - t_phase, 3)
+        t_phase = now
+
+    meta = {}
+    mark("init")
     salt = 0
     load_weights(salt)
+    mark("write")
     order = list(range(len(entries)))[:: -1 if args.hook_order == "reverse" else 1]
     consume = torch.cuda.Stream() if args.cross_stream else None
     scratch = torch.zeros(64, device="cuda")
@@ -265,7 +278,8 @@ def main():
         torch.cuda.synchronize()
         submissions += 1
 
-    records, meta = [], {}
+    mark("warmup_graph")
+    records = []
     if args.profile:
         selected = rank == args.profile_rank
         prof = (torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU,
@@ -309,7 +323,9 @@ def main():
             verdict[frame] = verify(outputs, indices, on_gpu=True)  # no host sync inside the loop
             submissions += 1
         pending = not torch.cuda.current_stream().query()
+        t_sync = time.perf_counter_ns()
         torch.cuda.synchronize()
+        meta.update(final_sync_ms=(time.perf_counter_ns() - t_sync) / 1e6)
         assert int(verdict.sum()) == 0, f"GPU verdicts: {verdict.tolist()}"
         meta.update(async_check=True, per_forward_host_syncs=0, pending_after_enqueue=pending)
     else:
@@ -342,6 +358,9 @@ def main():
                                 indices_sha256=hashlib.sha256(indices.cpu().numpy().tobytes()).hexdigest(),
                                 data_ok=True, scale_ok=True))
             dist.barrier(group=control)
+    mark("measure")
+    if args.impl == "native":
+        meta.update(error_state=buffer.error_state())
     meta.update(
         impl=args.impl, route=args.route, routing=buffer.get_route_info(), dtype=args.dtype, entries=entries,
         tokens=args.tokens, capacity=capacity, hook_order=args.hook_order, cross_stream=args.cross_stream,
@@ -353,6 +372,7 @@ def main():
     root.mkdir(parents=True, exist_ok=True)
     (root / f"engram-r{rank}.json").write_text(json.dumps(dict(metadata=meta, samples=records), indent=2,
                                                            default=str))
+    print(f"rank {rank}: phases {meta['phase_s']}", flush=True)
     timed = [r["e2e_ms"] for r in records if r.get("e2e_ms") and not r.get("warmup")]
     if timed:
         timed.sort()

@@ -99,85 +99,190 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid
         p.layer_arrivals[layer] = 0;
 }
 
-__global__ void __launch_bounds__(kPushThreads) push_kernel(const __grid_constant__ PushParams p) {
-    __shared__ uint32_t s_last;
-    // Locate this block's task (blocks are laid out task after task).
-    uint32_t t = 0;
-    while (t + 1 < p.num_tasks && p.tasks[t + 1].first_block <= blockIdx.x)
-        ++t;
-    const PushTask task = p.tasks[t];
-    const uint32_t block_in_task = blockIdx.x - task.first_block;
-    const uint32_t lo = block_in_task * task.rows_per_block;
-    const uint32_t hi = min(lo + task.rows_per_block, task.rows);
-    const uint32_t task_blocks = (task.rows + task.rows_per_block - 1) / task.rows_per_block;
-
-    const uint64_t *inbox = p.inbox + (uint64_t(task.requester) * p.layers + task.layer) * p.capacity;
-    uint8_t *out = reinterpret_cast<uint8_t *>(p.out_base[task.requester]) +
-                   uint64_t(task.layer) * p.capacity * p.row_bytes;
-    const uint32_t vectors = p.row_bytes / 16;
-    constexpr uint32_t kRowsPerStep = kPushThreads / kPushLanesPerRow;
-    constexpr int kUnroll = 4;
-    const uint32_t sub = threadIdx.x / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
-
-    for (uint32_t base = lo; base < hi; base += kRowsPerStep * kUnroll) {
-        const uint8_t *src[kUnroll];
-        uint8_t *dst[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const uint32_t i = base + u * kRowsPerStep + sub;
-            src[u] = nullptr;
-            dst[u] = nullptr;
-            if (i < hi) {
-                const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + i);
-                const uint32_t row = uint32_t(entry), pos = uint32_t(entry >> 32);
-                if (row < p.table_rows && pos < p.capacity) {
-                    src[u] = p.table + uint64_t(row) * p.row_bytes;
-                    dst[u] = out + uint64_t(pos) * p.row_bytes;
-                } else if (vlane == 0) {
-                    report_error(p.error, kPushBounds, task.layer, task.requester, entry, p.table_rows);
-                }
-            }
-        }
-        for (uint32_t chunk = 0; chunk < vectors; chunk += kPushLanesPerRow) {
-            Vec16 buf[kUnroll];
-            const uint32_t v = chunk + vlane;
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-                if (src[u] != nullptr && v < vectors)
-                    buf[u] = ld_nc_na_v4(src[u] + uint64_t(v) * 16);
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-                if (dst[u] != nullptr && v < vectors)
-                    st_v4(dst[u] + uint64_t(v) * 16, buf[u]);
-        }
-    }
-    // The last block of the task releases the requester's done flag after every
-    // block's peer stores are visible system-wide.
-    fence_sc_sys();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t *counter = p.arrivals + uint64_t(task.requester) * p.layers + task.layer;
-        s_last = atom_add_acq_rel_gpu(counter, 1u) == task_blocks - 1;
-        if (s_last) {
-            *counter = 0;
-            fence_sc_sys();
-            auto *done = reinterpret_cast<uint64_t *>(p.done_base[task.requester]) +
-                         (uint64_t(task.layer) * p.world + p.rank);
-            st_release_sys_u64(done, task.epoch);
-        }
+// ------------------------------------------------------------------ serving
+// Claims the next chunk of request (r, l, epoch): -1 when the request is not
+// the one armed in `claim` or every chunk is taken.
+__device__ __forceinline__ int32_t claim_chunk(uint64_t *claim, uint64_t epoch, uint32_t chunks) {
+    unsigned long long *word = reinterpret_cast<unsigned long long *>(claim);
+    unsigned long long old = atomicAdd(word, 0ull);
+    while (true) {
+        if ((old >> 32) != epoch - 1 || uint32_t(old) >= chunks)
+            return -1;
+        const unsigned long long seen = atomicCAS(word, old, old + 1);
+        if (seen == old)
+            return int32_t(uint32_t(old));
+        old = seen;
     }
 }
 
-__global__ void hook_wait_kernel(const __grid_constant__ HookParams p) {
-    for (uint32_t owner = threadIdx.x; owner < p.world; owner += blockDim.x) {
-        const uint32_t slot = p.layer * p.world + owner;
-        if (p.totals[slot] == 0)
+// Whole-CTA worker: copies chunks of request (r, l, epoch) from this rank's
+// host shard to the requester's output until none is left.  Returns true if
+// it copied anything.  Every thread of the CTA must call it.
+__device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint64_t epoch, uint32_t rows) {
+    __shared__ int32_t s_chunk;
+    const uint32_t slot = r * s.layers + l;
+    const uint32_t chunks = (rows + s.chunk_rows - 1) / s.chunk_rows;
+    const uint64_t *inbox = s.inbox + uint64_t(slot) * s.capacity;
+    uint8_t *out = reinterpret_cast<uint8_t *>(s.out_base[r]) + uint64_t(l) * s.capacity * s.row_bytes;
+    const uint32_t vectors = s.row_bytes / 16;
+    constexpr uint32_t kRowsPerStep = kPushThreads / kPushLanesPerRow;
+    constexpr int kUnroll = 4;
+    const uint32_t sub = threadIdx.x / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
+    bool worked = false;
+    while (true) {
+        if (threadIdx.x == 0)
+            s_chunk = claim_chunk(s.claim + slot, epoch, chunks);
+        __syncthreads();
+        const int32_t c = s_chunk;
+        __syncthreads();
+        if (c < 0 || s.out_base[r] == 0)
+            break;
+        worked = true;
+        const uint32_t lo = uint32_t(c) * s.chunk_rows, hi = min(lo + s.chunk_rows, rows);
+        for (uint32_t base = lo; base < hi; base += kRowsPerStep * kUnroll) {
+            const uint8_t *src[kUnroll];
+            uint8_t *dst[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const uint32_t i = base + u * kRowsPerStep + sub;
+                src[u] = nullptr;
+                dst[u] = nullptr;
+                if (i < hi) {
+                    const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + i);
+                    const uint32_t row = uint32_t(entry), pos = uint32_t(entry >> 32);
+                    if (row < s.table_rows && pos < s.capacity) {
+                        src[u] = s.table + uint64_t(row) * s.row_bytes;
+                        dst[u] = out + uint64_t(pos) * s.row_bytes;
+                    } else if (vlane == 0) {
+                        report_error(s.error, kPushBounds, l, r, entry, s.table_rows);
+                    }
+                }
+            }
+            for (uint32_t chunk = 0; chunk < vectors; chunk += kPushLanesPerRow) {
+                Vec16 buf[kUnroll];
+                const uint32_t v = chunk + vlane;
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u)
+                    if (src[u] != nullptr && v < vectors)
+                        buf[u] = ld_nc_na_v4(src[u] + uint64_t(v) * 16);
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u)
+                    if (dst[u] != nullptr && v < vectors)
+                        st_v4(dst[u] + uint64_t(v) * 16, buf[u]);
+            }
+        }
+        // This chunk's peer stores become visible system-wide before it counts.
+        fence_sc_sys();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long *fin = reinterpret_cast<unsigned long long *>(s.finish + slot);
+            const unsigned long long prev = atomicAdd(fin, 1ull);
+            if (uint32_t(prev) + 1 == chunks) {
+                // Last chunk: re-arm both words for epoch + 1, then release done.
+                *reinterpret_cast<volatile unsigned long long *>(s.claim + slot) = epoch << 32;
+                *reinterpret_cast<volatile unsigned long long *>(fin) = epoch << 32;
+                fence_sc_sys();
+                auto *done = reinterpret_cast<uint64_t *>(s.done_base[r]) + (uint64_t(l) * s.world + s.rank);
+                st_release_sys_u64(done, epoch);
+            }
+        }
+    }
+    return worked;
+}
+
+// Launched by the owner service for the requests it found in the mailbox.
+// Requests another worker already finished are skipped by the claim.
+__global__ void __launch_bounds__(kPushThreads) push_kernel(const __grid_constant__ PushParams p) {
+    for (uint32_t t = 0; t < p.num_tasks; ++t) {
+        const PushTask &task = p.tasks[t];
+        serve_request(p.s, task.requester, task.layer, task.epoch, task.rows);
+    }
+}
+
+// Copies this rank's mailbox (host memory) into the device board; warp 0 of
+// block 0 only, so the polling costs one PCIe read per slot per pass.
+__device__ __forceinline__ void refresh_board(const ServeParams &s) {
+    const uint32_t slots = s.world * s.layers;
+    for (uint32_t i = threadIdx.x; i < slots; i += 32) {
+        const uint32_t r = i / s.layers;
+        if (!((s.serve_mask >> r) & 1ull))
             continue;
-        const uint64_t expected = p.epochs[slot];
-        bool timed_out = false;
-        const uint64_t seen = wait_flag_eq(p.done + slot, expected, p.timeout_ns, &timed_out);
-        if (timed_out)
-            report_error(p.error, kWaitTimeout, p.layer, owner, seen, expected);
+        const MailboxHeader *h = s.headers + i;
+        const uint64_t epoch = ld_acquire_sys_u64(&h->ready);
+        if (epoch == 0)
+            continue;
+        const uint32_t rows = *reinterpret_cast<const volatile uint32_t *>(&h->rows);
+        *reinterpret_cast<volatile unsigned long long *>(s.board + i) = (epoch << 32) | rows;
+    }
+}
+
+// Hook kernel: waits until every host-route owner of `layer` that received a
+// request has released the expected epoch.  While it waits, all its CTAs serve
+// requests addressed to this rank, so two ranks whose hooks wait on each other
+// always make progress without depending on another kernel being scheduled.
+__global__ void __launch_bounds__(kPushThreads) hook_kernel(const __grid_constant__ HookParams p) {
+    __shared__ int32_t s_state;
+    __shared__ uint64_t s_task;
+    const ServeParams &s = p.s;
+    const uint64_t start = global_timer_ns();
+    uint32_t backoff = 64;
+    while (true) {
+        if (threadIdx.x == 0) {
+            int32_t state = 1;  // 1: all done, 0: waiting, 2: timed out
+            for (uint32_t o = 0; o < s.world; ++o) {
+                const uint32_t slot = p.layer * s.world + o;
+                if (p.totals[slot] == 0)
+                    continue;
+                const uint64_t expected = p.epochs[slot];
+                const uint64_t seen = ld_acquire_sys_u64(p.done + slot);
+                if (seen != expected) {
+                    state = 0;
+                    if (global_timer_ns() - start > p.timeout_ns) {
+                        report_error(s.error, kWaitTimeout, p.layer, o, seen, expected);
+                        state = 2;
+                    }
+                    break;
+                }
+            }
+            s_state = state;
+        }
+        __syncthreads();
+        if (s_state != 0)
+            return;
+        __syncthreads();
+        bool worked = false;
+        if (p.serve) {
+            if (blockIdx.x == 0 && threadIdx.x < 32)
+                refresh_board(s);
+            __syncthreads();
+            const uint32_t slots = s.world * s.layers;
+            for (uint32_t i = 0; i < slots; ++i) {
+                if (threadIdx.x == 0) {
+                    uint64_t task = 0;
+                    if ((s.serve_mask >> (i / s.layers)) & 1ull) {
+                        const uint64_t b = *reinterpret_cast<const volatile unsigned long long *>(s.board + i);
+                        const uint64_t epoch = b >> 32;
+                        const uint32_t rows = uint32_t(b);
+                        const uint64_t armed = *reinterpret_cast<const volatile unsigned long long *>(s.claim + i);
+                        const uint32_t chunks = (rows + s.chunk_rows - 1) / s.chunk_rows;
+                        if (epoch != 0 && rows != 0 && (armed >> 32) == epoch - 1 && uint32_t(armed) < chunks)
+                            task = b;
+                    }
+                    s_task = task;
+                }
+                __syncthreads();
+                const uint64_t task = s_task;
+                __syncthreads();
+                if (task != 0)
+                    worked |= serve_request(s, i / s.layers, i % s.layers, task >> 32, uint32_t(task));
+            }
+        }
+        if (!worked) {
+            __nanosleep(backoff);
+            backoff = backoff < 2048 ? backoff * 2 : 2048;
+        } else {
+            backoff = 64;
+        }
     }
 }
 
@@ -231,7 +336,9 @@ cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream) {
 }
 
 cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream) {
-    hook_wait_kernel<<<1, 64, 0, stream>>>(p);
+    // Serving needs enough CTAs to keep host-memory reads in flight; a rank
+    // that serves nobody only waits.
+    hook_kernel<<<p.serve ? 16 : 1, kPushThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -105,34 +105,49 @@ struct DispatchParams {
 };
 
 struct PushTask {
-    uint32_t requester, layer, rows, first_block;
-    uint32_t rows_per_block, channels;
+    uint32_t requester, layer, rows, channels;
     uint64_t epoch;
 };
 
-// Owner-side push: copy the requested rows from this rank's host shard (read
-// zero-copy) into each requester's output (peer stores), then release the
-// requester's done flag once every CTA of that task has finished.
-struct PushParams {
-    const uint8_t *table;         // this rank's host shard, mapped for this GPU
-    const uint64_t *inbox;        // this rank's inbox region [world][layers][capacity]
-    uint32_t *arrivals;           // [world][layers] scratch
+// Owner-side serving state shared by the push kernel (launched by the owner
+// service) and the hook kernel (which serves inbound requests while it waits).
+// A request (requester r, layer l, epoch e) is split into chunks of
+// `chunk_rows` rows.  Workers claim chunks with a CAS on claim[r][l] and count
+// finished chunks on finish[r][l]; both words hold ((e - 1) << 32) | count
+// while epoch e is served.  The worker that finishes the last chunk re-arms
+// both words for epoch e + 1 and only then releases done = e at the
+// requester, so a request is executed exactly once whoever runs it.
+struct ServeParams {
+    const uint8_t *table;             // this rank's host shard, mapped for this GPU
+    const uint64_t *inbox;            // this rank's inbox [world][layers][capacity]
+    uint64_t *claim;                  // [world][layers]
+    uint64_t *finish;                 // [world][layers]
+    uint64_t *board;                  // [world][layers] (epoch << 32) | rows seen in the mailbox
+    const MailboxHeader *headers;     // this rank's mailbox headers (host memory, device-visible)
     ErrorSink error;
     uint64_t out_base[kMaxRanks];     // requester arena output region (mapping)
     uint64_t done_base[kMaxRanks];    // requester arena done region (mapping)
-    PushTask tasks[kMaxPushTasks];
-    uint32_t num_tasks, layers, world, rank, capacity, row_bytes;
+    uint64_t serve_mask;              // bit r: requester r reaches me through the host route
+    uint32_t layers, world, rank, capacity, row_bytes, chunk_rows;
     uint64_t table_rows;
+};
+
+// Owner-side push for the requests the owner service found.
+struct PushParams {
+    ServeParams s;
+    PushTask tasks[kMaxPushTasks];
+    uint32_t num_tasks;
 };
 
 // Hook-side wait for one layer: every host-route owner that received a
 // non-empty request must publish the matching epoch in done[layer][owner].
+// While waiting, the kernel also serves requests addressed to this rank.
 struct HookParams {
+    ServeParams s;
     const uint32_t *totals;
     const uint64_t *epochs;
-    const uint64_t *done;         // this rank's done region [layers][world]
-    ErrorSink error;
-    uint32_t layer, world;
+    const uint64_t *done;             // this rank's done region [layers][world]
+    uint32_t layer, serve;
     uint64_t timeout_ns;
 };
 

@@ -96,8 +96,13 @@ void OwnerService::loop() {
             if (!batch.empty()) {
                 requests_.fetch_add(batch.size(), std::memory_order_relaxed);
                 batches_.fetch_add(1, std::memory_order_relaxed);
+                const auto t0 = std::chrono::steady_clock::now();
                 launcher_(batch);
                 last_work = std::chrono::steady_clock::now();
+                const uint64_t us = uint64_t(
+                    std::chrono::duration_cast<std::chrono::microseconds>(last_work - t0).count());
+                if (us > max_launch_us_.load(std::memory_order_relaxed))
+                    max_launch_us_.store(us, std::memory_order_relaxed);
                 continue;
             }
             const auto idle = std::chrono::steady_clock::now() - last_work;

@@ -43,6 +43,9 @@ namespace engram {
 
 enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
 
+// Rows per claimable unit of an owner-push request.
+constexpr uint32_t kServeChunkRows = 128;
+
 namespace {
 
 template <class T> T get(const py::dict &d, const char *key) {
@@ -368,12 +371,12 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         }
         if (has_host_routes_ && tokens_ > 0) {
             HookParams h{};
+            h.s = serve_params_;
             h.totals = totals_;
             h.epochs = epochs_;
             h.done = reinterpret_cast<const uint64_t *>(arena_->ptr() + dev_done_);
-            h.error = sink();
             h.layer = layer;
-            h.world = world_;
+            h.serve = serves_any_ ? 1 : 0;
             h.timeout_ns = timeout_ns_;
             check_cuda(launch_hook_wait(h, s), "launch hook wait");
             ++launches_;
@@ -419,6 +422,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["served_requests"] = service_.requests();
         d["served_rows"] = service_.rows();
         d["push_batches"] = service_.batches();
+        d["max_push_launch_us"] = service_.max_launch_us();
         d["egm_enabled"] = egm_;
         bool direct_remote = false;
         for (uint32_t p = 0; p < world_; ++p)
@@ -579,7 +583,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         totals_ = reinterpret_cast<uint32_t *>(take(lw * 4));
         cursors_ = reinterpret_cast<uint32_t *>(take(lw * 4));
         layer_arrivals_ = reinterpret_cast<uint32_t *>(take(layers_ * 4));
-        push_arrivals_ = reinterpret_cast<uint32_t *>(take(lw * 4));
+        claim_ = reinterpret_cast<uint64_t *>(take(lw * 8));
+        finish_ = reinterpret_cast<uint64_t *>(take(lw * 8));
+        board_ = reinterpret_cast<uint64_t *>(take(lw * 8));
         dev_error_ = reinterpret_cast<ErrorRecord *>(take(sizeof(ErrorRecord)));
         check(at <= dev_scratch_bytes_, "scratch region too small");
     }
@@ -656,46 +662,47 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d.rank = rank_;
         d.tile_rows = 512;
 
-        PushParams &p = push_template_;
-        p = PushParams{};
-        p.table = reinterpret_cast<const uint8_t *>(host_->ptr() + host_table_);
-        p.inbox = reinterpret_cast<const uint64_t *>(arena + dev_inbox_);
-        p.arrivals = push_arrivals_;
-        p.error = sink();
+        ServeParams &v = serve_params_;
+        v = ServeParams{};
+        v.table = reinterpret_cast<const uint8_t *>(host_->ptr() + host_table_);
+        v.inbox = reinterpret_cast<const uint64_t *>(arena + dev_inbox_);
+        v.claim = claim_;
+        v.finish = finish_;
+        v.board = board_;
+        v.headers = reinterpret_cast<const MailboxHeader *>(host_->ptr() + host_headers_);
+        v.error = sink();
         for (uint32_t r = 0; r < world_; ++r) {
             const bool serve = r != rank_ && routes_[r] == kHostRoute;
-            p.out_base[r] = serve ? peer_dev_[r]->ptr() + dev_output_ : 0;
-            p.done_base[r] = serve ? peer_dev_[r]->ptr() + dev_done_ : 0;
+            v.out_base[r] = serve ? peer_dev_[r]->ptr() + dev_output_ : 0;
+            v.done_base[r] = serve ? peer_dev_[r]->ptr() + dev_done_ : 0;
+            if (serve)
+                v.serve_mask |= 1ull << r;
         }
-        p.layers = layers_;
-        p.world = world_;
-        p.rank = rank_;
-        p.capacity = capacity_;
-        p.row_bytes = row_bytes_;
-        p.table_rows = table_rows_;
+        v.layers = layers_;
+        v.world = world_;
+        v.rank = rank_;
+        v.capacity = capacity_;
+        v.row_bytes = row_bytes_;
+        v.chunk_rows = kServeChunkRows;
+        v.table_rows = table_rows_;
     }
 
-    // Runs on the owner-service thread.
+    // Runs on the owner-service thread: one push kernel per batch of up to
+    // kMaxPushTasks requests; its CTAs claim chunks of every request in turn.
     void launch_push_batch(const std::vector<PushTask> &batch) {
         size_t at = 0;
         while (at < batch.size()) {
-            PushParams p = push_template_;
+            PushParams p{};
+            p.s = serve_params_;
             const size_t n = std::min(batch.size() - at, size_t(kMaxPushTasks));
-            uint32_t blocks = 0;
+            uint32_t chunks = 0, channels = 1;
             for (size_t i = 0; i < n; ++i) {
-                PushTask t = batch[at + i];
-                const uint32_t ch = std::max(1u, std::min(t.channels, 16u));
-                const uint32_t max_blocks = ch * 16;
-                uint32_t want = (t.rows + 63) / 64;
-                want = std::max(1u, std::min(want, max_blocks));
-                uint32_t rpb = (t.rows + want - 1) / want;
-                rpb = (rpb + 63) / 64 * 64;
-                t.rows_per_block = rpb;
-                t.first_block = blocks;
-                blocks += (t.rows + rpb - 1) / rpb;
-                p.tasks[i] = t;
+                p.tasks[i] = batch[at + i];
+                chunks += (p.tasks[i].rows + kServeChunkRows - 1) / kServeChunkRows;
+                channels = std::max(channels, std::min(p.tasks[i].channels, 16u));
             }
             p.num_tasks = uint32_t(n);
+            const uint32_t blocks = std::max(1u, std::min(chunks, channels * 8));
             check_cuda(launch_push(p, int(blocks), owner_stream_), "launch push");
             at += n;
         }
@@ -769,7 +776,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     std::unique_ptr<FdServer> fd_server_;
     long fds_served_ = 0;
     uint64_t *epochs_ = nullptr;
-    uint32_t *totals_ = nullptr, *cursors_ = nullptr, *layer_arrivals_ = nullptr, *push_arrivals_ = nullptr;
+    uint32_t *totals_ = nullptr, *cursors_ = nullptr, *layer_arrivals_ = nullptr;
+    uint64_t *claim_ = nullptr, *finish_ = nullptr, *board_ = nullptr;
     ErrorRecord *dev_error_ = nullptr, *host_error_ = nullptr, *host_error_dev_ = nullptr;
     // routes
     std::vector<int> routes_;
@@ -779,7 +787,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     bool has_host_routes_ = false, serves_any_ = false;
     GatherParams gather_{};
     DispatchParams dispatch_{};
-    PushParams push_template_{};
+    ServeParams serve_params_{};
     // streams and events
     cudaEvent_t issued_ = nullptr, capture_issued_ = nullptr;
     std::vector<cudaEvent_t> finished_;

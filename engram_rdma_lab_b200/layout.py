@@ -162,9 +162,9 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) 
         ("sf_output", L * align(c.max_tokens, 4) * c.ept * P * 4),
         ("done", L * W * 8),
         ("inbox", W * L * c.capacity * 8),
-        # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32,
-        # layer_arrivals[L] u32, push_arrivals[W*L] u32, push_epochs[W*L] u64
-        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + W * L * 4 + W * L * 8 + 256),
+        # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32, layer_arrivals[L] u32,
+        # serve claim/finish/board [W*L] u64 each, device error record, alignment slack
+        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 256),
     ]
     off = 0
     for name, size in regions:
