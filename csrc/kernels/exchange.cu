@@ -338,7 +338,7 @@ cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream) {
 cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream) {
     // Serving needs enough CTAs to keep host-memory reads in flight; a rank
     // that serves nobody only waits.
-    hook_kernel<<<p.serve ? 16 : 1, kPushThreads, 0, stream>>>(p);
+    hook_kernel<<<p.serve ? 8 : 1, kPushThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -44,7 +44,7 @@ namespace engram {
 enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
 
 // Rows per claimable unit of an owner-push request.
-constexpr uint32_t kServeChunkRows = 128;
+constexpr uint32_t kServeChunkRows = 256;
 
 namespace {
 
@@ -702,7 +702,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 channels = std::max(channels, std::min(p.tasks[i].channels, 16u));
             }
             p.num_tasks = uint32_t(n);
-            const uint32_t blocks = std::max(1u, std::min(chunks, channels * 8));
+            const uint32_t blocks = std::max(1u, std::min(chunks, std::max(4u, channels * 2)));
             check_cuda(launch_push(p, int(blocks), owner_stream_), "launch push");
             at += n;
         }
