@@ -70,11 +70,14 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid
             }
         }
     }
-    // Publish this CTA's peer stores system-wide before arriving.
-    fence_sc_sys();
+    // Publish this CTA's peer stores system-wide before arriving: the barrier
+    // orders every thread's stores before thread 0, whose system-scope fence
+    // is cumulative over them.
     __syncthreads();
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
+        fence_sc_sys();
         s_last = atom_add_acq_rel_gpu(p.layer_arrivals + layer, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
     if (!s_last)
         return;
@@ -171,10 +174,11 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
                         st_v4(dst[u] + uint64_t(v) * 16, buf[u]);
             }
         }
-        // This chunk's peer stores become visible system-wide before it counts.
-        fence_sc_sys();
+        // This chunk's peer stores become visible system-wide before it counts
+        // (barrier, then one cumulative system-scope fence).
         __syncthreads();
         if (threadIdx.x == 0) {
+            fence_sc_sys();
             unsigned long long *fin = reinterpret_cast<unsigned long long *>(s.finish + slot);
             const unsigned long long prev = atomicAdd(fin, 1ull);
             if (uint32_t(prev) + 1 == chunks) {
