@@ -80,7 +80,7 @@ def parse():
     p.add_argument("--cuda-graph", action="store_true")
     p.add_argument("--async-check", action="store_true")
     p.add_argument("--async-eager", action="store_true")
-    p.add_argument("--overlap-gemm", type=int, default=0, help="M=N=K... of a bf16 GEMM on another stream (0 = off)")
+    p.add_argument("--overlap-gemm", default="", help="M,N,K of a bf16 GEMM overlapped on another stream (empty = off)")
     p.add_argument("--profile", action="store_true")
     p.add_argument("--profile-rank", type=int, default=0)
     p.add_argument("--egm-fail-pair", type=parse_pair, action="append", default=[])
@@ -173,10 +173,9 @@ def main():
     phase = torch.zeros((), dtype=torch.int32, device="cuda")
     gemm = None
     if args.overlap_gemm:
-        n = args.overlap_gemm
-        gemm = (torch.randn(n, n, device="cuda", dtype=torch.bfloat16), torch.randn(n, n, device="cuda",
-                                                                                    dtype=torch.bfloat16),
-                torch.cuda.Stream())
+        m, n, k = (int(v) for v in args.overlap_gemm.split(","))
+        gemm = (torch.randn(m, k, device="cuda", dtype=torch.bfloat16),
+                torch.randn(k, n, device="cuda", dtype=torch.bfloat16), torch.cuda.Stream())
 
     def advance_locality(indices):
         # GPU-side phase: 0 self, 1 layer0 padding + others remote, 2 all padding,
