@@ -84,6 +84,7 @@ def parse():
     p.add_argument("--profile", action="store_true")
     p.add_argument("--profile-rank", type=int, default=0)
     p.add_argument("--egm-fail-pair", type=parse_pair, action="append", default=[])
+    p.add_argument("--verify-every", type=int, default=1, help="check every K-th timed round (0 = never)")
     p.add_argument("--timeout", type=float, default=60.0, help="bounded GPU wait per hook, seconds")
     p.add_argument("--output-dir", required=True)
     a = p.parse_args()
@@ -240,7 +241,7 @@ def main():
         submissions += 1
     torch.cuda.synchronize()
     if active:
-        assert int(verify(outputs, indices)) == 0, "warm-up outputs differ from the oracle"
+        assert int(verify(outputs, indices, on_gpu=True)) == 0, "warm-up outputs differ from the oracle"
 
     if args.check_errors and active:
         hooks = buffer.fetch(indices)
@@ -350,12 +351,14 @@ def main():
             torch.cuda.synchronize()
             elapsed = (time.perf_counter_ns() - start) / 1e6
             submissions += 1
-            assert int(verify(outputs, indices)) == 0, f"round {it}: outputs differ from the oracle"
+            checked = args.verify_every > 0 and (it < 0 or it % args.verify_every == 0)
+            if checked:
+                assert int(verify(outputs, indices, on_gpu=True)) == 0, f"round {it}: outputs differ from the oracle"
             nbytes = len(entries) * indices.shape[1] * args.ept * args.hidden * dtype.itemsize
             records.append(dict(rank=rank, round=it, warmup=it < 0, requester_active=True, bytes=nbytes,
                                 e2e_ms=elapsed, gbps=nbytes / elapsed / 1e6 if elapsed else None,
                                 indices_sha256=hashlib.sha256(indices.cpu().numpy().tobytes()).hexdigest(),
-                                data_ok=True, scale_ok=True))
+                                data_ok=True if checked else None, scale_ok=True if checked else None))
             dist.barrier(group=control)
     mark("measure")
     if args.impl == "native":
