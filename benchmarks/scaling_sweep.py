@@ -44,7 +44,7 @@ def measure(buf, entries, tokens, ept, dist_name, rank, world, steps, warmup, fl
         b.synchronize()
         if k >= warmup:
             times.append(a.elapsed_time(b))
-    t = torch.tensor(times, dtype=torch.float64)
+    t = torch.tensor(times, dtype=torch.float64, device="cuda")
     gathered = [torch.zeros_like(t) for _ in range(world)]
     dist.all_gather(gathered, t)
     per_step = torch.stack(gathered).max(dim=0).values.tolist()
