@@ -118,9 +118,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         dev_scratch_ = off("dev_scratch");
         dev_scratch_bytes_ = off("dev_scratch_bytes");
         device_bytes_ = off("device_bytes");
-        host_table_ = off("host_table");
-        host_headers_ = off("host_headers");
-        host_bytes_ = off("host_bytes");
+        table_bytes_ = off("table_bytes");
+        mailbox_bytes_ = off("mailbox_bytes");
         check(!egm_ || dev_mirror_bytes_ == table_rows_ * row_bytes_, "mirror size does not match the vocabulary");
 
         c10::cuda::CUDAGuard guard(device_);
@@ -128,7 +127,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         check_cuda(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_), "SM count");
         try {
             arena_ = SharedAllocation::device(device_bytes_, device_);
-            host_ = SharedAllocation::host(host_bytes_, device_, allow_host_vmm_);
+            host_ = SharedAllocation::host(table_bytes_, device_, allow_host_vmm_);
+            mailbox_ = SharedAllocation::host(mailbox_bytes_, device_, allow_host_vmm_);
             carve_scratch();
             check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&host_error_), sizeof(ErrorRecord), cudaHostAllocMapped),
                        "error record");
@@ -161,20 +161,20 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     py::dict bootstrap() {
         check(!closed_, "runtime closed");
         if (!fd_server_)
-            fd_server_ = std::make_unique<FdServer>(socket_name(rank_), std::vector<int>{host_->fd(), arena_->fd()});
+            fd_server_ = std::make_unique<FdServer>(socket_name(rank_), std::vector<int>{mailbox_->fd(), arena_->fd()});
         py::dict d;
         d["pid"] = int(getpid());
         d["socket"] = socket_name(rank_);
-        d["host_kind"] = int(host_->kind());
-        d["host_kind_name"] = memory_kind_name(host_->kind());
-        d["host_bytes"] = host_->bytes();
-        d["host_numa"] = host_->numa();
+        d["host_kind"] = int(mailbox_->kind());
+        d["host_kind_name"] = memory_kind_name(mailbox_->kind());
+        d["host_bytes"] = mailbox_->bytes();
+        d["host_numa"] = mailbox_->numa();
         d["dev_bytes"] = arena_->bytes();
         d["mirror"] = egm_;
         d["mirror_offset"] = dev_mirror_;
         d["mirror_bytes"] = egm_ ? dev_mirror_bytes_ : size_t(0);
         d["config"] = py::make_tuple(world_, local_size_, entries_, hidden_, elem_, max_tokens_, ept_, packs_, egm_,
-                                     local_sf_, device_bytes_, host_bytes_);
+                                     local_sf_, device_bytes_, table_bytes_, mailbox_bytes_);
         return d;
     }
 
@@ -198,7 +198,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                                                           get<int>(d, "host_numa"));
             peer_dev_[p] = std::make_unique<PeerMapping>(MemoryKind::DeviceVmm, fetch_fd(sock, 1),
                                                          get<size_t>(d, "dev_bytes"), device_, -1);
-            check(peer_dev_[p]->bytes() >= device_bytes_ && peer_host_[p]->bytes() >= host_bytes_,
+            check(peer_dev_[p]->bytes() >= device_bytes_ && peer_host_[p]->bytes() >= mailbox_bytes_,
                   "peer allocation smaller than the agreed plan");
             if (candidates[p] != kPeerHbm)
                 continue;
@@ -261,8 +261,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             c.layers = layers_;
             c.capacity = capacity_;
             c.rank = rank_;
-            c.headers = reinterpret_cast<const MailboxHeader *>(static_cast<uint8_t *>(host_->host_ptr()) +
-                                                                host_headers_);
+            c.headers = reinterpret_cast<const MailboxHeader *>(mailbox_->host_ptr());
             c.serve = serve_;
             const int dev = device_;
             service_.start(
@@ -280,7 +279,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         c10::cuda::CUDAGuard guard(device_);
         const size_t bytes = size_t(entries_[layer]) * row_bytes_;
         check(size_t(storage.nbytes()) == bytes && storage.is_contiguous(), "storage shape");
-        uint8_t *dst = static_cast<uint8_t *>(host_->host_ptr()) + host_table_ + size_t(table_bases_[layer]) * row_bytes_;
+        uint8_t *dst = static_cast<uint8_t *>(host_->host_ptr()) + size_t(table_bases_[layer]) * row_bytes_;
         if (storage.is_cuda())
             check_cuda(cudaMemcpy(dst, storage.data_ptr(), bytes, cudaMemcpyDefault), "write vocabulary to host shard");
         else
@@ -412,7 +411,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         py::dict d;
         d["rank"] = rank_;
         d["device_allocation_bytes"] = arena_ ? arena_->bytes() : 0;
-        d["host_allocation_bytes"] = host_ ? host_->bytes() : 0;
+        d["host_allocation_bytes"] = (host_ ? host_->bytes() : 0) + (mailbox_ ? mailbox_->bytes() : 0);
         d["output_bytes"] = size_t(layers_) * capacity_ * row_bytes_;
         d["cpu_vocabulary_bytes"] = size_t(table_rows_) * row_bytes_;
         d["hbm_mirror_bytes"] = egm_ ? dev_mirror_bytes_ : size_t(0);
@@ -618,7 +617,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.layer = lt;
         for (uint32_t o = 0; o < world_; ++o) {
             if (o == rank_)
-                g.direct_base[o] = egm_ ? arena + dev_mirror_ : host_->ptr() + host_table_;
+                g.direct_base[o] = egm_ ? arena + dev_mirror_ : host_->ptr();
             else if (routes_[o] == kPeerHbm)
                 g.direct_base[o] = peer_dev_[o]->ptr() + dev_mirror_;
             else
@@ -654,7 +653,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         for (uint32_t o = 0; o < world_; ++o) {
             const bool host = o != rank_ && routes_[o] == kHostRoute;
             d.inbox_base[o] = host ? peer_dev_[o]->ptr() + dev_inbox_ : 0;
-            d.header_base[o] = host ? peer_host_[o]->ptr() + host_headers_ : 0;
+            d.header_base[o] = host ? peer_host_[o]->ptr() : 0;
         }
         d.layers = layers_;
         d.capacity = capacity_;
@@ -664,12 +663,12 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
 
         ServeParams &v = serve_params_;
         v = ServeParams{};
-        v.table = reinterpret_cast<const uint8_t *>(host_->ptr() + host_table_);
+        v.table = reinterpret_cast<const uint8_t *>(host_->ptr());
         v.inbox = reinterpret_cast<const uint64_t *>(arena + dev_inbox_);
         v.claim = claim_;
         v.finish = finish_;
         v.board = board_;
-        v.headers = reinterpret_cast<const MailboxHeader *>(host_->ptr() + host_headers_);
+        v.headers = reinterpret_cast<const MailboxHeader *>(mailbox_->ptr());
         v.error = sink();
         for (uint32_t r = 0; r < world_; ++r) {
             const bool serve = r != rank_ && routes_[r] == kHostRoute;
@@ -752,6 +751,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             cudaFreeHost(host_error_);
             host_error_ = nullptr;
         }
+        mailbox_.reset();
         host_.reset();
         arena_.reset();
     }
@@ -769,9 +769,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     std::string token_;
     size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
            dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;
-    size_t host_table_ = 0, host_headers_ = 0, host_bytes_ = 0;
+    size_t table_bytes_ = 0, mailbox_bytes_ = 0;
     // memory
-    std::unique_ptr<SharedAllocation> arena_, host_;
+    std::unique_ptr<SharedAllocation> arena_, host_, mailbox_;
     std::vector<std::unique_ptr<PeerMapping>> peer_host_, peer_dev_;
     std::unique_ptr<FdServer> fd_server_;
     long fds_served_ = 0;

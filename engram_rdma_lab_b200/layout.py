@@ -1,11 +1,12 @@
 """Per-rank memory plan shared by the native runtime and the torch oracle.
 
-Every rank owns two exportable allocations:
+Every rank owns three allocations (the mailbox and the arena are exported):
 
 * a **host shard** (pinned host memory, CUDA-VMM ``HOST_NUMA`` when the driver
-  supports it): the vocabulary rows of every layer back to back, followed by the
-  mailbox headers that requesters' GPUs write and this rank's owner service
-  polls;
+  supports it): the vocabulary rows of every layer back to back, read only by
+  this rank's GPU;
+* a small **host mailbox**: the request headers that requesters' GPUs write
+  and this rank's owner service polls (the only host memory peers map);
 * a **device arena** (one CUDA-VMM ``DEVICE`` allocation): the optional HBM
   mirror of the vocabulary, the FP8 scale table, the per-layer output region,
   the scale output, the per-(layer, owner) done flags, the request inbox that
@@ -120,6 +121,8 @@ class MemoryPlan:
     host: dict = field(default_factory=dict)
     device_bytes: int = 0
     host_bytes: int = 0
+    table_bytes: int = 0
+    mailbox_bytes: int = 0
     sf_bases: list = field(default_factory=list)
     sf_rows_per_layer: list = field(default_factory=list)
 
@@ -131,6 +134,8 @@ class MemoryPlan:
         out.update({f"host_{k}_bytes": int(v[1]) for k, v in self.host.items()})
         out["device_bytes"] = int(self.device_bytes)
         out["host_bytes"] = int(self.host_bytes)
+        out["table_bytes"] = int(self.table_bytes)
+        out["mailbox_bytes"] = int(self.mailbox_bytes)
         return out
 
 
@@ -172,11 +177,13 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) 
         off = align(off + max(size, 0), REGION_ALIGN)
     plan.device_bytes = align(max(off, REGION_ALIGN), ALLOC_ALIGN)
 
-    off = 0
-    for name, size in [("table", c.table_rows * c.row_bytes), ("headers", W * L * HEADER_BYTES)]:
-        plan.host[name] = (off, size)
-        off = align(off + size, REGION_ALIGN)
-    plan.host_bytes = align(off, ALLOC_ALIGN)
+    # Host memory: the vocabulary shard (read only by this rank's GPU) and, in a
+    # separate small allocation that every peer maps, the mailbox headers.
+    plan.host["table"] = (0, c.table_rows * c.row_bytes)
+    plan.host["headers"] = (0, W * L * HEADER_BYTES)
+    plan.table_bytes = align(max(c.table_rows * c.row_bytes, 1), ALLOC_ALIGN)
+    plan.mailbox_bytes = align(W * L * HEADER_BYTES, ALLOC_ALIGN)
+    plan.host_bytes = plan.table_bytes + plan.mailbox_bytes
     return plan
 
 

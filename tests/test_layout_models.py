@@ -56,6 +56,7 @@ def test_plan_regions_disjoint_and_aligned(mirror, local_sf):
     assert plan.device["mirror"][1] == (cfg.table_rows * 256 if mirror else 0)
     assert plan.device["output"][1] == 2 * 4096 * 24 * 256
     assert plan.host["table"][1] == cfg.table_rows * 256
+    assert plan.host_bytes == plan.table_bytes + plan.mailbox_bytes and plan.mailbox_bytes < (4 << 20)
     sf_rows = sum(n * (8 if local_sf else 1) for n in cfg.entries)
     assert plan.device["sf_table"][1] == sf_rows * 2 * 4
     assert storage_size_hint([524288, 524309], 256, 4096, 24, torch.float8_e4m3fn, 2, 8, mirror, local_sf) == (
