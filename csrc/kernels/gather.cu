@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     const uint32_t t0 = blockIdx.x * tiles_per_cta;
     const uint32_t t1 = min(t0 + tiles_per_cta, total_tiles);
 
+    const uint32_t epoch = p.dedup ? dedup_epoch(p.dedup_state) : 0;
     if (warp == 0) {
         // Producer: classify the tile's rows and issue one bulk copy per direct
         // row.  Indices arrive through a kIndexDepth-tile cp.async ring, so
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
                     if (owner >= p.world) {
                         zero = true;
                         report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
-                    } else if (s_direct[owner] != 0) {
+                    } else if (s_direct[owner] != 0 &&
+                               !(p.dedup && dedup_duplicate(p, layer * p.rows + start + lane, epoch))) {
                         const uint64_t row = uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n);
                         src = reinterpret_cast<const uint8_t *>(s_direct[owner]) + row * p.row_bytes;
                     }
@@ -264,6 +266,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     const uint32_t warp_id = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const uint32_t warp_stride = gridDim.x * (blockDim.x / 32);
 
+    const uint32_t epoch = p.dedup ? dedup_epoch(p.dedup_state) : 0;
     int32_t x_next = -1;
     if (warp_id < groups) {
         const uint32_t item = warp_id * 32 + lane;
@@ -293,7 +296,10 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                 if (owner >= p.world) {
                     report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
                 } else if (s_direct[owner] != 0) {
-                    src = s_direct[owner] + (uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n)) * p.row_bytes;
+                    if (p.dedup && dedup_duplicate(p, item, epoch))
+                        dst = 0;  // a repeat: copied from its first occurrence after the gather
+                    else
+                        src = s_direct[owner] + (uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n)) * p.row_bytes;
                 } else {
                     dst = 0;  // host route: the owner pushes this row
                 }

@@ -85,6 +85,34 @@ struct GatherParams {
     uint32_t variant;             // kGatherBulk or kGatherSimt
     uint32_t ctas_per_sm;         // SIMT grid cap per SM (0 = default 2)
     uint32_t unroll;              // SIMT row-steps in flight for 256-byte rows (0 = default)
+    // Request deduplication (see DedupParams): when `dedup` is set, an item whose
+    // slot's elected first occurrence is another item is skipped here and
+    // copied locally by the expand kernel afterwards.
+    uint32_t dedup;
+    const uint32_t *dedup_slots;  // [layers * rows] table slot per item, kDedupNone if not deduplicated
+    const uint64_t *dedup_vals;   // [table] (epoch << 32) | ~first_item
+    const uint32_t *dedup_state;  // [0] epoch of the previous fetch
+};
+
+constexpr uint32_t kDedupNone = 0xFFFFFFFFu;
+
+// Per-fetch request deduplication for direct-route rows.  keys/vals form an
+// open-addressing table of `table_mask + 1` slots that is never cleared:
+// keys carry the fetch epoch in bits 36-63 (layer in 31-35, row id in 0-30),
+// so entries of older fetches read as empty.  vals hold (epoch << 32) |
+// (0xFFFFFFFF - item) and are combined with atomicMax, which elects the
+// smallest item of the current epoch as the key's first occurrence.
+struct DedupParams {
+    const int32_t *indices;
+    uint64_t *keys;
+    uint64_t *vals;
+    uint32_t *slots;              // [layers * rows]
+    uint32_t *state;              // [0] last epoch, [1] uniques, [2] items, [3] arrivals
+    uint32_t *host_stats;         // host-mapped: [0] uniques, [1] items, [2] epoch of the last finished fetch
+    uint8_t *output;
+    LayerTable layer;
+    uint64_t direct_base[kMaxRanks];
+    uint32_t layers, rows, world, table_mask, capacity, row_bytes;
 };
 
 // Requester-side dispatch for host-route owners: append (row, position) pairs
@@ -158,6 +186,9 @@ cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream);
 cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream);
 // 16-byte streaming copy (peer-bandwidth diagnostics).
 cudaError_t launch_stream_copy(const void *src, void *dst, uint64_t bytes, int blocks, cudaStream_t stream);
+// Request deduplication around the gather (dedup.cu).
+cudaError_t launch_dedup(const DedupParams &p, int num_sms, cudaStream_t stream);
+cudaError_t launch_expand(const DedupParams &p, int num_sms, cudaStream_t stream);
 // Bounded wait on a flag nothing sets; used by the timeout self-test.
 cudaError_t launch_wait_probe(const uint64_t *flag, uint64_t expected, uint64_t timeout_ns, ErrorSink error,
                               cudaStream_t stream);

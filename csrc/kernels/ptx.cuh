@@ -185,6 +185,22 @@ __device__ __forceinline__ Vec16 ld_shared_v4(const void *p) {
     return v;
 }
 
+// Epoch of the fetch in flight for request deduplication (dedup.cu).
+__device__ __forceinline__ uint32_t dedup_epoch(const uint32_t *state) {
+    const uint32_t e = (state[0] + 1) & ((1u << 28) - 1);
+    return e == 0 ? 1 : e;
+}
+
+// True if `item` repeats an earlier request of this fetch (its row arrives by
+// a local copy from the first occurrence instead of the gather).
+__device__ __forceinline__ bool dedup_duplicate(const GatherParams &p, uint32_t item, uint32_t epoch) {
+    const uint32_t slot = __ldcg(p.dedup_slots + item);
+    if (slot == kDedupNone)
+        return false;
+    const uint64_t v = __ldcg(reinterpret_cast<const unsigned long long *>(p.dedup_vals) + slot);
+    return (v >> 32) == epoch && (0xFFFFFFFFu - uint32_t(v)) != item;
+}
+
 // Poll `flag` until it equals `expected` or `timeout_ns` passes.  Returns the
 // last value read.  Never traps; the caller reports a timeout.
 __device__ __forceinline__ uint64_t wait_flag_eq(const void *flag, uint64_t expected, uint64_t timeout_ns,

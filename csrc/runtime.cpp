@@ -85,6 +85,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         gather_choice_ = get<std::string>(cfg, "gather_kernel");
         gather_variant_ = gather_choice_ == "bulk" ? kGatherBulk : kGatherSimt;
         tuning_ctas_per_sm_ = get<uint32_t>(cfg, "gather_ctas_per_sm");
+        dedup_mode_ = get<int>(cfg, "dedup");
         tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
@@ -115,6 +116,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         dev_sf_output_ = off("dev_sf_output");
         dev_done_ = off("dev_done");
         dev_inbox_ = off("dev_inbox");
+        dev_dedup_ = off("dev_dedup");
+        dev_dedup_bytes_ = off("dev_dedup_bytes");
         dev_scratch_ = off("dev_scratch");
         dev_scratch_bytes_ = off("dev_scratch_bytes");
         device_bytes_ = off("device_bytes");
@@ -135,6 +138,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             std::memset(host_error_, 0, sizeof(ErrorRecord));
             check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&host_error_dev_), host_error_, 0),
                        "error record device pointer");
+            check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&dedup_stats_), 16, cudaHostAllocMapped), "dedup stats");
+            std::memset(dedup_stats_, 0, 16);
+            check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&dedup_stats_dev_), dedup_stats_, 0),
+                       "dedup stats device pointer");
             check_cuda(cudaEventCreateWithFlags(&issued_, cudaEventDisableTiming), "issue event");
             check_cuda(cudaEventCreateWithFlags(&capture_issued_, cudaEventDisableTiming), "capture event");
             for (uint32_t l = 0; l < layers_; ++l) {
@@ -334,7 +341,18 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 check_cuda(launch_dispatch(d, s), "launch dispatch");
                 ++launches_;
             }
+            const bool dedup = use_dedup();
+            DedupParams dp{};
+            if (dedup) {
+                dp = dedup_;
+                dp.indices = idx;
+                dp.rows = rows;
+                check_cuda(launch_dedup(dp, num_sms_, s), "launch dedup");
+                ++launches_;
+                ++dedup_fetches_;
+            }
             GatherParams g = gather_;
+            g.dedup = dedup ? 1 : 0;
             g.indices = idx;
             g.rows = rows;
             g.tokens = tokens_;
@@ -344,6 +362,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             g.col_major_sf = col_major ? 1 : 0;
             check_cuda(launch_gather(g, num_sms_, s), "launch gather");
             ++launches_;
+            if (dedup) {
+                check_cuda(launch_expand(dp, num_sms_, s), "launch expand");
+                ++launches_;
+            }
         }
         if (issue_captured_) {
             check_cuda(cudaEventRecord(capture_issued_, s), "record capture issue");
@@ -442,6 +464,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["kernel_launches"] = launches_;
         d["num_sms"] = num_sms_;
         d["gather_kernel"] = gather_variant_ == kGatherSimt ? "simt" : "tma_bulk";
+        d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
+        d["dedup_fetches"] = dedup_fetches_;
+        d["dedup_last_unique_ratio"] = dedup_ratio_;
         return d;
     }
 
@@ -586,6 +611,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         finish_ = reinterpret_cast<uint64_t *>(take(lw * 8));
         board_ = reinterpret_cast<uint64_t *>(take(lw * 8));
         dev_error_ = reinterpret_cast<ErrorRecord *>(take(sizeof(ErrorRecord)));
+        dedup_state_ = reinterpret_cast<uint32_t *>(take(16));
         check(at <= dev_scratch_bytes_, "scratch region too small");
     }
 
@@ -639,6 +665,27 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.packs = packs_;
         g.sf_warps = packs_ ? 2 : 0;
         g.variant = gather_variant_;
+        const uint32_t slots = dev_dedup_bytes_ ? uint32_t((dev_dedup_bytes_ - size_t(layers_) * capacity_ * 4) / 16) : 0;
+        g.dedup_slots = reinterpret_cast<const uint32_t *>(arena + dev_dedup_ + size_t(slots) * 16);
+        g.dedup_vals = reinterpret_cast<const uint64_t *>(arena + dev_dedup_ + size_t(slots) * 8);
+        g.dedup_state = dedup_state_;
+        DedupParams &dd = dedup_;
+        dd = DedupParams{};
+        dd.keys = reinterpret_cast<uint64_t *>(arena + dev_dedup_);
+        dd.vals = reinterpret_cast<uint64_t *>(arena + dev_dedup_ + size_t(slots) * 8);
+        dd.slots = reinterpret_cast<uint32_t *>(arena + dev_dedup_ + size_t(slots) * 16);
+        dd.state = dedup_state_;
+        dd.host_stats = dedup_stats_dev_;
+        dd.output = reinterpret_cast<uint8_t *>(arena + dev_output_);
+        dd.layer = lt;
+        for (uint32_t o = 0; o < world_; ++o)
+            dd.direct_base[o] = g.direct_base[o];
+        dd.layers = layers_;
+        dd.world = world_;
+        dd.table_mask = slots ? slots - 1 : 0;
+        dd.capacity = capacity_;
+        dd.row_bytes = row_bytes_;
+        dedup_slots_ = slots;
         g.ctas_per_sm = tuning_ctas_per_sm_;
         g.unroll = tuning_unroll_;
 
@@ -751,6 +798,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             cudaFreeHost(host_error_);
             host_error_ = nullptr;
         }
+        if (dedup_stats_) {
+            cudaFreeHost(dedup_stats_);
+            dedup_stats_ = nullptr;
+        }
         mailbox_.reset();
         host_.reset();
         arena_.reset();
@@ -766,6 +817,44 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
     uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0;
     std::string gather_choice_ = "auto";
+    // request deduplication: mode 0 off, 1 on, 2 auto (on while the last
+    // measured unique ratio is below kDedupOnRatio; re-measured every
+    // kDedupProbeEvery fetches while off)
+    int dedup_mode_ = 2;
+    size_t dev_dedup_ = 0, dev_dedup_bytes_ = 0;
+    uint32_t *dedup_state_ = nullptr, *dedup_stats_ = nullptr, *dedup_stats_dev_ = nullptr;
+    uint32_t dedup_slots_ = 0, dedup_seen_epoch_ = 0, dedup_since_probe_ = 0;
+    double dedup_ratio_ = -1.0;
+    uint64_t dedup_fetches_ = 0;
+    DedupParams dedup_{};
+    static constexpr double kDedupOnRatio = 0.75;
+    static constexpr uint32_t kDedupProbeEvery = 32;
+
+    bool use_dedup() {
+        if (dedup_mode_ == 0 || dedup_slots_ == 0)
+            return false;
+        // Fold in the counts of the last finished deduplicated fetch (host-mapped,
+        // written by the GPU; read without synchronising).
+        volatile uint32_t *st = dedup_stats_;
+        const uint32_t epoch = st[2];
+        if (epoch != dedup_seen_epoch_) {
+            const uint32_t uniques = st[0], items = st[1];
+            dedup_seen_epoch_ = epoch;
+            if (items > 0)
+                dedup_ratio_ = double(uniques) / double(items);
+        }
+        if (dedup_mode_ == 1)
+            return true;
+        if (dedup_ratio_ < 0.0 || dedup_ratio_ < kDedupOnRatio) {
+            dedup_since_probe_ = 0;
+            return true;
+        }
+        if (++dedup_since_probe_ >= kDedupProbeEvery) {
+            dedup_since_probe_ = 0;
+            return true;
+        }
+        return false;
+    }
     std::string token_;
     size_t dev_mirror_ = 0, dev_mirror_bytes_ = 0, dev_sf_table_ = 0, dev_output_ = 0, dev_sf_output_ = 0, dev_done_ = 0,
            dev_inbox_ = 0, dev_scratch_ = 0, dev_scratch_bytes_ = 0, device_bytes_ = 0;

@@ -95,6 +95,19 @@ def _gather_kernel() -> str:
     return value
 
 
+def _dedup_mode() -> int:
+    """``ENGRAM_DEDUP``: ``auto`` (default), ``1`` or ``0``.
+
+    Deduplication moves each distinct requested row once per fetch and copies
+    repeats locally; ``auto`` enables it while the last measured distinct ratio
+    is below 0.75 and re-measures periodically.
+    """
+    value = os.environ.get("ENGRAM_DEDUP", "auto")
+    if value not in ("auto", "0", "1"):
+        raise ValueError("ENGRAM_DEDUP must be 'auto', '0' or '1'")
+    return {"0": 0, "1": 1, "auto": 2}[value]
+
+
 class EngramBuffer(EngramBufferBase):
     """Native B200 EngramBuffer (peer-HBM and host-push routes)."""
 
@@ -172,7 +185,8 @@ class EngramBuffer(EngramBufferBase):
         """
         egm = EgmConfig.from_env().enabled
         return storage_size_hint(num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype,
-                                 num_sf_packs, group.size(), egm, env_flag("ENGRAM_WRITE_LOCAL_SF", egm))
+                                 num_sf_packs, group.size(), egm, env_flag("ENGRAM_WRITE_LOCAL_SF", egm),
+                                 _dedup_mode() != 0)
 
     @staticmethod
     def get_theoretical_config(group, num_layers, num_max_tokens, num_entries_per_token,
@@ -188,7 +202,7 @@ class EngramBuffer(EngramBufferBase):
             raise RuntimeError("Buffer is destroyed")
         cfg = self._check_config_args(num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype,
                                       num_sf_packs)
-        plan = plan_memory(cfg, self.num_ranks, self.egm.enabled, self.local_sf)
+        plan = plan_memory(cfg, self.num_ranks, self.egm.enabled, self.local_sf, _dedup_mode() != 0)
         if plan.device_bytes > self.num_gpu_bytes or plan.host_bytes > self.num_rdma_storage_bytes:
             raise ValueError("Insufficient capacity: use EngramBuffer.get_storage_size_hint")
         tokens = [None] * self.num_ranks
@@ -203,6 +217,7 @@ class EngramBuffer(EngramBufferBase):
             gather_kernel=_gather_kernel(),
             gather_ctas_per_sm=env_int("ENGRAM_GATHER_CTAS_PER_SM", 0, minimum=0),
             gather_unroll=env_int("ENGRAM_GATHER_UNROLL", 0, minimum=0),
+            dedup=_dedup_mode(),
         )
         native = None
         with torch.cuda.device(self.device):

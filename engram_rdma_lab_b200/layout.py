@@ -139,7 +139,13 @@ class MemoryPlan:
         return out
 
 
-def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) -> MemoryPlan:
+def dedup_table_slots(config: EngramConfig) -> int:
+    """Slots of the request-deduplication table: a power of two >= 2x the requests."""
+    need = max(1024, 2 * config.layers * config.capacity)
+    return 1 << (need - 1).bit_length()
+
+
+def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, dedup: bool = True) -> MemoryPlan:
     """Lay out one rank's host shard and device arena.
 
     ``mirror``: keep an HBM copy of the vocabulary for the peer-HBM route.
@@ -167,9 +173,11 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) 
         ("sf_output", L * align(c.max_tokens, 4) * c.ept * P * 4),
         ("done", L * W * 8),
         ("inbox", W * L * c.capacity * 8),
+        # dedup: keys[H] u64 + vals[H] u64 + slots[L * capacity] u32
+        ("dedup", (dedup_table_slots(c) * 16 + L * c.capacity * 4) if dedup else 0),
         # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32, layer_arrivals[L] u32,
         # serve claim/finish/board [W*L] u64 each, device error record, alignment slack
-        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 256),
+        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 16 + 256),
     ]
     off = 0
     for name, size in regions:
@@ -187,9 +195,9 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool) 
     return plan
 
 
-def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf):
+def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf, dedup=True):
     cfg = validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world)
-    plan = plan_memory(cfg, world, mirror, local_sf)
+    plan = plan_memory(cfg, world, mirror, local_sf, dedup)
     return plan.device_bytes, plan.host_bytes
 
 

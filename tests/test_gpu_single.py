@@ -197,3 +197,54 @@ def test_native_extension_is_in_tree():
     mod = _native.load()
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     assert os.path.realpath(mod.__file__).startswith(os.path.realpath(root))
+
+
+@pytest.mark.parametrize("kernel", ["simt", "bulk"])
+@pytest.mark.parametrize("mode", ["1", "auto"])
+def test_dedup_on_skewed_requests(kernel, mode, monkeypatch):
+    monkeypatch.setenv("ENGRAM_DEDUP", mode)
+    monkeypatch.setenv("ENGRAM_GATHER_KERNEL", kernel)
+    entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 1024, ept, dtype, packs, True)
+    storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda")
+    buf.write(storages, scales)
+    for epoch in range(4):
+        idx = make_indices(0, 1, entries, 1024 - 100 * epoch, ept, epoch=epoch, distribution="zipf", padding=0.03,
+                           device="cuda")
+        outs = [h() for h in buf.fetch(idx)]
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs)
+    idx = make_indices(0, 1, entries, 1024, ept, epoch=9, distribution="zipf", device="cuda")
+    [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n = torch.tensor(entries, device="cuda", dtype=torch.int32)[:, None, None]
+    with torch.cuda.graph(graph):
+        idx.add_(1).remainder_(n)
+        outs = [h() for h in buf.fetch(idx)]
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs)
+    del graph
+    mem = buf.memory_usage()
+    assert mem["dedup_fetches"] >= 4
+    assert 0 < mem["dedup_last_unique_ratio"] < 0.75
+    buf.destroy()
+
+
+def test_dedup_auto_turns_off_for_uniform_requests(monkeypatch):
+    monkeypatch.setenv("ENGRAM_DEDUP", "auto")
+    entries, hidden, ept = (200003, 200009), 128, 8
+    buf = make_buffer(entries, hidden, 512, ept, torch.bfloat16, 0, True)
+    storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+    buf.write(storages)
+    for epoch in range(10):
+        idx = make_indices(0, 1, entries, 512, ept, epoch=epoch, device="cuda")
+        outs = [h() for h in buf.fetch(idx)]
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, torch.bfloat16, 0)
+    mem = buf.memory_usage()
+    assert mem["dedup_last_unique_ratio"] > 0.9
+    assert mem["dedup_fetches"] <= 2  # measured once, then off until the next probe
+    buf.destroy()
