@@ -69,8 +69,10 @@ def _peer_hbm(rank, world):
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")
         buf.write(storages, scales)
         dist.barrier()
-        for epoch in range(3):
-            idx = make_indices(rank, world, entries, 512, ept, epoch=epoch, padding=0.02, device="cuda")
+        for epoch in range(4):
+            dist_name = "zipf" if epoch == 3 else "uniform"  # skewed requests exercise deduplication
+            idx = make_indices(rank, world, entries, 512, ept, epoch=epoch, padding=0.02, distribution=dist_name,
+                               device="cuda")
             outs = [h() for h in buf.fetch(idx, use_tma_aligned_col_major_sf=epoch != 1)]
             torch.cuda.synchronize()
             _check(outs, idx, entries, hidden, dtype, packs, col_major=epoch != 1)
