@@ -828,7 +828,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t dedup_fetches_ = 0;
     DedupParams dedup_{};
     static constexpr double kDedupOnRatio = 0.75;
-    static constexpr uint32_t kDedupProbeEvery = 32;
+    static constexpr uint32_t kDedupProbeEvery = 256;
 
     bool use_dedup() {
         if (dedup_mode_ == 0 || dedup_slots_ == 0)
