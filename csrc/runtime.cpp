@@ -19,6 +19,7 @@
 // under capture an internal event joins cross-stream hooks into the graph and
 // EXTERNAL events carry completion to work outside the graph.
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
@@ -148,6 +149,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 cudaEvent_t e;
                 check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "layer event");
                 finished_.push_back(e);
+                finished_stream_.push_back(nullptr);
             }
             int lo = 0, hi = 0;
             check_cuda(cudaDeviceGetStreamPriorityRange(&lo, &hi), "stream priorities");
@@ -324,9 +326,21 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
         issue_captured_ = capturing(s);
         issue_stream_ = s;
+        // An eager fetch reuses the output region: wait for the previous
+        // round's layer completions, unless they were recorded on this very
+        // stream outside a capture (stream order already covers them).
         if (!issue_captured_)
-            for (auto e : finished_)
-                check_cuda(cudaStreamWaitEvent(s, e, 0), "workspace reuse dependency");
+            for (uint32_t l = 0; l < layers_; ++l)
+                if (finished_stream_[l] != s)
+                    check_cuda(cudaStreamWaitEvent(s, finished_[l], 0), "workspace reuse dependency");
+        try {
+            // The kernels read `indices` on this stream: keep the caching
+            // allocator from recycling it before they finish.
+            c10::cuda::CUDACachingAllocator::recordStream(indices.storage().data_ptr(),
+                                                          at::cuda::getCurrentCUDAStream(device_));
+        } catch (const c10::Error &) {
+            // Not from the caching allocator: the caller owns its lifetime.
+        }
         tokens_ = uint32_t(indices.size(1));
         const uint32_t rows = tokens_ * ept_;
         uint32_t ts, hs, ls;
@@ -374,7 +388,12 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             check_cuda(cudaEventRecord(issued_, s), "record issue");
         }
         ++fetches_;
-        return make_outputs(ts, hs, ls);
+        if (tokens_ != cached_tokens_ || col_major != cached_col_major_ || cached_outputs_.size() == 0) {
+            cached_outputs_ = make_outputs(ts, hs, ls);
+            cached_tokens_ = tokens_;
+            cached_col_major_ = col_major;
+        }
+        return py::list(cached_outputs_);
     }
 
     void wait_layer(uint32_t layer) {
@@ -402,8 +421,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             check_cuda(launch_hook_wait(h, s), "launch hook wait");
             ++launches_;
         }
-        check_cuda(cudaEventRecordWithFlags(finished_[layer], s, capturing(s) ? cudaEventRecordExternal : 0),
+        const bool hook_captured = capturing(s);
+        check_cuda(cudaEventRecordWithFlags(finished_[layer], s, hook_captured ? cudaEventRecordExternal : 0),
                    "record layer completion");
+        finished_stream_[layer] = hook_captured ? nullptr : s;
     }
 
     // ------------------------------------------------------------- inspection
@@ -570,6 +591,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     void close() {
         if (closed_)
             return;
+        // The cached views keep this runtime alive; drop them so the memory
+        // is released once the caller's own references are gone.
+        cached_outputs_ = py::list();
         {
             c10::cuda::CUDAGuard guard(device_);
             cudaError_t rc = cudaDeviceSynchronize();
@@ -880,6 +904,11 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     // streams and events
     cudaEvent_t issued_ = nullptr, capture_issued_ = nullptr;
     std::vector<cudaEvent_t> finished_;
+    std::vector<cudaStream_t> finished_stream_;  // stream of the last eager hook per layer
+    // Output views of the last (tokens, scale layout); rebuilt when either changes.
+    py::list cached_outputs_;
+    uint32_t cached_tokens_ = 0xFFFFFFFFu;
+    bool cached_col_major_ = true;
     cudaStream_t issue_stream_ = nullptr, owner_stream_ = nullptr;
     bool issue_captured_ = false;
     uint32_t tokens_ = 0;

@@ -305,12 +305,12 @@ class EngramBuffer(EngramBufferBase):
             raise ValueError("num_qps exceeds the allocated channels")
         generation = self._begin_fetch()
         try:
+            # The runtime records `indices` on the current stream for the allocator.
             outputs = self.runtime.fetch(indices, qps, bool(use_tma_aligned_col_major_sf))
         except Exception:
             self._pending = set()
             raise
         self._input = indices
-        indices.record_stream(torch.cuda.current_stream(self.device))
         return self._make_hooks(generation, self.runtime.wait_layer, outputs)
 
     # -------------------------------------------------------------- inspection
