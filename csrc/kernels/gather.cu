@@ -33,12 +33,13 @@ constexpr int kBulkThreads = 128;       // producer warp, consumer warp, 2 scale
 constexpr uint32_t kStageTargetBytes = 64 * 1024;
 constexpr uint64_t kPipelineTimeoutNs = 2000000000ull;
 constexpr uint32_t kIndexDepth = 8;     // tiles of indices in flight per producer
+constexpr uint32_t kIndexAhead = 4;     // SIMT: groups of indices in flight per warp
 
 struct StageMeta {
     uint32_t layer, start, count, direct_mask, zero_mask, pad[3];
 };
 
-// Scale warps shared by both variants: `lanes` threads starting at `lane_id`
+// Scale warps of the TMA variant: `lanes` threads starting at `lane_id`
 // gather the scales of every (layer, row) item, 4 items in flight per lane.
 __device__ __forceinline__ void gather_scales(const GatherParams &p, const uint64_t *s_sf, const uint32_t *s_entries,
                                               const uint32_t *s_sfbase, uint32_t lane_id, uint32_t lanes) {
@@ -54,17 +55,13 @@ __device__ __forceinline__ void gather_scales(const GatherParams &p, const uint6
             out[u] = nullptr;
             if (item >= total)
                 continue;
+            // Items run in index order in both scale layouts, so the index
+            // reads coalesce (they cross PCIe when the indices sit in pinned
+            // host memory); column-major stores scatter 4 B each and merge in L2.
             const uint32_t layer = item / p.rows;
             const uint32_t r = item - layer * p.rows;
-            uint32_t token, slot;
-            if (p.col_major_sf) {
-                slot = r / p.tokens;
-                token = r - slot * p.tokens;
-            } else {
-                token = r / p.ept;
-                slot = r - token * p.ept;
-            }
-            const int32_t x = __ldg(p.indices + layer * p.rows + token * p.ept + slot);
+            const uint32_t token = r / p.ept, slot = r - token * p.ept;
+            const int32_t x = __ldg(p.indices + item);
             out[u] = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
                      uint64_t(slot) * p.packs * p.sf_hidden_stride;
             if (x >= 0) {
@@ -248,10 +245,11 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 // item l once (owner, source, destination, scales) and the copy loop hands the
 // 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
 // per-row integer work is done by one lane instead of LPR lanes.  The next
-// group's indices are loaded before this group's rows, hiding that latency.
+// kIndexAhead groups' indices are loaded before this group's rows, hiding that latency.
 template <int LPR, int VPL, int UNROLL>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
+    __shared__ int32_t s_index[kSimtThreads / 32][kIndexAhead * 32];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
     load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
     __syncthreads();
@@ -267,19 +265,28 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     const uint32_t warp_stride = gridDim.x * (blockDim.x / 32);
 
     const uint32_t epoch = p.dedup ? dedup_epoch(p.dedup_state) : 0;
-    int32_t x_next = -1;
-    if (warp_id < groups) {
-        const uint32_t item = warp_id * 32 + lane;
-        x_next = item < total ? __ldg(p.indices + item) : -1;
+    // The indices of this warp's next kIndexAhead groups are in flight at
+    // once, copied by cp.async into a per-warp shared ring.  Their completion
+    // is tracked apart from the row loads' registers, so a row copy never
+    // waits on a later group's index (a PCIe round trip when the indices sit
+    // in pinned host memory).  Each lane reads back only what it copied.
+    int32_t *ring = s_index[threadIdx.x / 32];
+#pragma unroll
+    for (uint32_t a = 0; a < kIndexAhead; ++a) {
+        const uint32_t ga = warp_id + a * warp_stride;
+        const uint32_t item = ga * 32 + lane;
+        if (ga < groups && item < total)
+            cp_async_4(ring + a * 32 + lane, p.indices + item);
+        else
+            *reinterpret_cast<volatile int32_t *>(ring + a * 32 + lane) = -1;
+        cp_async_commit();
     }
-    for (uint32_t g = warp_id; g < groups; g += warp_stride) {
+    uint32_t k = 0;
+    for (uint32_t g = warp_id; g < groups; g += warp_stride, ++k) {
         const uint32_t item = g * 32 + lane;
-        const int32_t x = x_next;
-        const uint32_t g_next = g + warp_stride;
-        if (g_next < groups) {
-            const uint32_t nitem = g_next * 32 + lane;
-            x_next = nitem < total ? __ldg(p.indices + nitem) : -1;
-        }
+        cp_async_wait<kIndexAhead - 1>();  // group k has landed
+        int32_t *slot_x = ring + (k % kIndexAhead) * 32 + lane;
+        const int32_t x = *reinterpret_cast<volatile int32_t *>(slot_x);
         // Resolve this lane's item; its scale loads are issued now and stored
         // after the rows, so their latency overlaps the row copies.
         uint64_t src = 0, dst = 0;  // src == 0 && dst != 0: zero row; dst == 0: not ours
@@ -319,6 +326,16 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                 for (uint32_t k = 0; k < kMaxPacksInFlight; ++k)
                     sf_val[k] = (sf_src != nullptr && k < p.packs) ? __ldg(sf_src + k) : 0.0f;
             }
+        }
+        // Refill the slot with group k + kIndexAhead (x is consumed above).
+        {
+            const uint32_t g_next = g + kIndexAhead * warp_stride;
+            const uint32_t nitem = g_next * 32 + lane;
+            if (g_next < groups && nitem < total)
+                cp_async_4(slot_x, p.indices + nitem);
+            else
+                *reinterpret_cast<volatile int32_t *>(slot_x) = -1;
+            cp_async_commit();
         }
         // Copy the group's rows: UNROLL row-steps x VPL vectors in flight per lane.
         for (uint32_t r0 = 0; r0 < 32; r0 += kRowsPerStep * UNROLL) {

@@ -18,6 +18,7 @@
 // eager fetch waits for the previous round's per-layer completion events;
 // under capture an internal event joins cross-stream hooks into the graph and
 // EXTERNAL events carry completion to work outside the graph.
+#include <ATen/core/CachingHostAllocator.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -314,13 +315,45 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     }
 
     // ------------------------------------------------------------------ fetch
+    // The kernels read `indices` on the current stream.  A device tensor is
+    // recorded on that stream for the caching allocator.  A pinned host
+    // tensor is read in place over PCIe through its device mapping (the
+    // step's H2D happens inside the kernels that consume it, with no copy
+    // engine round trip); its pinned block is recorded on the stream so the
+    // host allocator does not hand it out again before they finish.
+    const int32_t *index_pointer(const torch::Tensor &indices) {
+        auto stream = at::cuda::getCurrentCUDAStream(device_);
+        if (indices.is_cuda()) {
+            try {
+                c10::cuda::CUDACachingAllocator::recordStream(indices.storage().data_ptr(), stream);
+            } catch (const c10::Error &) {
+                // Not from the caching allocator: the caller owns its lifetime.
+            }
+            return indices.data_ptr<int32_t>();
+        }
+        if (indices.numel() == 0)
+            return nullptr;
+        const int32_t *host = indices.data_ptr<int32_t>();
+        cudaPointerAttributes attr{};
+        const bool mapped = cudaPointerGetAttributes(&attr, host) == cudaSuccess &&
+                            attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr;
+        if (!mapped) {
+            cudaGetLastError();
+            check(false, "host indices must be in pinned (page-locked, mapped) memory");
+        }
+        const auto &storage = indices.storage();
+        at::getHostAllocator(at::kCUDA)->record_event(storage.mutable_data(), storage.data_ptr().get_context(),
+                                                      stream.unwrap());
+        return static_cast<const int32_t *>(attr.devicePointer);
+    }
+
     py::list fetch(const torch::Tensor &indices, uint32_t channels, bool col_major) {
         check_health();
         check(connected_ && !closed_, "runtime is not connected");
-        check(indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_cuda() &&
-                  indices.is_contiguous() && indices.size(0) == layers_ && indices.size(2) == ept_ &&
-                  indices.size(1) <= max_tokens_ && indices.get_device() == device_,
-              "indices must be contiguous CUDA int32 [layers, tokens, ept]");
+        check(indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_contiguous() &&
+                  indices.size(0) == layers_ && indices.size(2) == ept_ && indices.size(1) <= max_tokens_ &&
+                  (indices.is_cpu() || (indices.is_cuda() && indices.get_device() == device_)),
+              "indices must be contiguous int32 [layers, tokens, ept] on this GPU or in pinned host memory");
         check(channels >= 1 && channels <= channels_, "channels exceed the allocation");
         c10::cuda::CUDAGuard guard(device_);
         cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
@@ -333,19 +366,11 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             for (uint32_t l = 0; l < layers_; ++l)
                 if (finished_stream_[l] != s)
                     check_cuda(cudaStreamWaitEvent(s, finished_[l], 0), "workspace reuse dependency");
-        try {
-            // The kernels read `indices` on this stream: keep the caching
-            // allocator from recycling it before they finish.
-            c10::cuda::CUDACachingAllocator::recordStream(indices.storage().data_ptr(),
-                                                          at::cuda::getCurrentCUDAStream(device_));
-        } catch (const c10::Error &) {
-            // Not from the caching allocator: the caller owns its lifetime.
-        }
+        const int32_t *idx = index_pointer(indices);
         tokens_ = uint32_t(indices.size(1));
         const uint32_t rows = tokens_ * ept_;
         uint32_t ts, hs, ls;
         sf_strides(tokens_, col_major, &ts, &hs, &ls);
-        const int32_t *idx = indices.data_ptr<int32_t>();
         if (rows > 0) {
             if (has_host_routes_) {
                 DispatchParams d = dispatch_;

@@ -91,7 +91,7 @@ class EngramBufferBase(ABC):
                 if sf.is_cuda and device_index is not None and sf.device.index != device_index:
                     raise ValueError("Scale CUDA tensor is on the wrong device")
 
-    def _check_fetch_args(self, indices, device_index, require_cuda: bool):
+    def _check_fetch_args(self, indices, device_index, require_cuda: bool, allow_pinned: bool = False):
         self._ready()
         if not self._written:
             raise RuntimeError("write() must initialize the vocabulary before fetch()")
@@ -108,9 +108,10 @@ class EngramBufferBase(ABC):
             and indices.is_contiguous()
         )
         if ok and require_cuda:
-            ok = indices.is_cuda and (device_index is None or indices.device.index == device_index)
+            on_device = indices.is_cuda and (device_index is None or indices.device.index == device_index)
+            ok = on_device or (allow_pinned and indices.device.type == "cpu" and indices.is_pinned())
         if not ok:
-            where = "CUDA " if require_cuda else ""
+            where = ("CUDA or pinned host " if allow_pinned else "CUDA ") if require_cuda else ""
             raise ValueError(
                 f"indices must be contiguous {where}int32 [layers, tokens, entries_per_token] within capacity"
             )

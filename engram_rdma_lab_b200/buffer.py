@@ -295,11 +295,15 @@ class EngramBuffer(EngramBufferBase):
     def fetch(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
         """Submit every layer's lookup on the current stream; return one hook per layer.
 
+        ``indices`` is int32 [layers, tokens, ept] on this GPU, or in pinned
+        host memory: then the kernels read it in place over PCIe (the step's
+        H2D is fused into the lookup) and the caller keeps it unchanged until
+        the hooks' work is done, as with any non-blocking copy.
         ``num_qps`` selects how many push channels host-route owners may use
         (0 = all allocated).  ``use_tma_aligned_col_major_sf`` selects the
         column-major, 4-aligned scale layout (default) or row-major.
         """
-        self._check_fetch_args(indices, self.device, require_cuda=True)
+        self._check_fetch_args(indices, self.device, require_cuda=True, allow_pinned=True)
         qps = num_qps or self.num_allocated_qps
         if not 1 <= qps <= self.num_allocated_qps:
             raise ValueError("num_qps exceeds the allocated channels")

@@ -22,7 +22,7 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
     "-Xptxas=-v" if os.environ.get("ENGRAM_PTXAS_VERBOSE") == "1" else "-Xptxas=-O3",
 ]
-CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-deprecated-declarations"]
+CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-deprecated-declarations", "-Wno-interference-size"]
 
 sources = [os.path.join("csrc", f) for f in ("runtime.cpp", "memory.cpp", "fdpass.cpp", "owner_service.cpp")]
 sources += [os.path.join("csrc", "kernels", f) for f in ("gather.cu", "exchange.cu", "dedup.cu", "noalloc.cu")]

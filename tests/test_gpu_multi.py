@@ -69,10 +69,12 @@ def _peer_hbm(rank, world):
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")
         buf.write(storages, scales)
         dist.barrier()
-        for epoch in range(4):
+        for epoch in range(5):
             dist_name = "zipf" if epoch == 3 else "uniform"  # skewed requests exercise deduplication
             idx = make_indices(rank, world, entries, 512, ept, epoch=epoch, padding=0.02, distribution=dist_name,
                                device="cuda")
+            if epoch == 4:  # pinned host indices, read in place by the kernels
+                idx = idx.cpu().pin_memory()
             outs = [h() for h in buf.fetch(idx, use_tma_aligned_col_major_sf=epoch != 1)]
             torch.cuda.synchronize()
             _check(outs, idx, entries, hidden, dtype, packs, col_major=epoch != 1)
@@ -105,6 +107,8 @@ def _host_route(rank, world):
     buf.write(storages)
     for epoch, tokens in enumerate([1024, 257, 1024]):
         idx = make_indices(rank, world, entries, tokens, ept, epoch=epoch, padding=0.03, device="cuda")
+        if epoch == 1:  # pinned host indices: dispatch and gather read them over PCIe
+            idx = idx.cpu().pin_memory()
         hooks = buf.fetch(idx)
         outs = [None, None]
         outs[1], outs[0] = hooks[1](), hooks[0]()

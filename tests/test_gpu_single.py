@@ -248,3 +248,59 @@ def test_dedup_auto_turns_off_for_uniform_requests(monkeypatch):
     assert mem["dedup_last_unique_ratio"] > 0.9
     assert mem["dedup_fetches"] <= 2  # measured once, then off until the next probe
     buf.destroy()
+
+
+def _pinned_view(idx, offset):
+    """``idx`` copied into a pinned block at an element offset (not 16-byte aligned for odd offsets)."""
+    block = torch.full((idx.numel() + offset,), -7, dtype=torch.int32).pin_memory()
+    host = block[offset:].view(idx.shape)
+    host.copy_(idx)
+    assert host.is_pinned() and host.is_contiguous()
+    return host
+
+
+@pytest.mark.parametrize("kernel", ["simt", "bulk"])
+@pytest.mark.parametrize("dedup", ["0", "1"])
+def test_pinned_host_indices_read_in_place(kernel, dedup, monkeypatch):
+    monkeypatch.setenv("ENGRAM_GATHER_KERNEL", kernel)
+    monkeypatch.setenv("ENGRAM_DEDUP", dedup)
+    entries, hidden, ept, dtype, packs = (5003, 5009), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 512, ept, dtype, packs, True)
+    try:
+        storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda")
+        buf.write(storages, scales)
+        for epoch, (tokens, col_major, offset) in enumerate([(300, True, 1001), (512, False, 0), (77, True, 3)]):
+            idx = make_indices(0, 1, entries, tokens, ept, epoch=epoch, padding=0.05,
+                               distribution="zipf" if dedup == "1" else "uniform")
+            host = _pinned_view(idx, offset)
+            outs = [h() for h in buf.fetch(host, use_tma_aligned_col_major_sf=col_major)]
+            torch.cuda.synchronize()
+            check(outs, idx, entries, hidden, dtype, packs, col_major=col_major)
+        with pytest.raises(ValueError, match="pinned host"):
+            buf.fetch(idx.clone())  # pageable host memory is refused before any launch
+    finally:
+        buf.destroy()
+
+
+def test_pinned_host_indices_under_graph_capture():
+    entries, hidden, ept = (4099, 4111), 128, 8
+    buf = make_buffer(entries, hidden, 256, ept, torch.bfloat16, 0, True)
+    try:
+        storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda")
+        buf.write(storages)
+        idx = make_indices(0, 1, entries, 256, ept, epoch=1)
+        host = _pinned_view(idx, 0)
+        [h() for h in buf.fetch(host)]
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = [h() for h in buf.fetch(host)]
+        for epoch in range(2, 4):  # the graph reads whatever the host buffer holds at replay
+            idx = make_indices(0, 1, entries, 256, ept, epoch=epoch)
+            host.copy_(idx)
+            graph.replay()
+            torch.cuda.synchronize()
+            check(outs, idx, entries, hidden, torch.bfloat16, 0)
+        del graph
+    finally:
+        buf.destroy()

@@ -158,3 +158,30 @@ def test_l2_flusher_and_percentile_on_cpu():
     assert int(f.sink) == 0
     assert percentile([1.0, 2.0, 3.0, 4.0], 0.5) == 2.5
     assert percentile([5.0], 0.99) == 5.0
+
+
+def test_numa_locality_from_fake_sysfs(tmp_path):
+    import os
+
+    from engram_rdma_lab_b200.utils.numa import bind_to_device_numa, device_locality, parse_cpulist
+
+    assert parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert parse_cpulist("") == set()
+    dev = tmp_path / "0000:1b:00.0"
+    dev.mkdir()
+    allowed = sorted(os.sched_getaffinity(0))
+    (dev / "numa_node").write_text("1\n")
+    (dev / "local_cpulist").write_text(f"{allowed[0]}\n")
+    assert device_locality("0000:1B:00.0", str(tmp_path)) == (1, {allowed[0]})
+    assert device_locality("0000:99:00.0", str(tmp_path)) == (-1, set())
+    before = os.sched_getaffinity(0)
+    try:
+        info = bind_to_device_numa(sysfs=str(tmp_path), address="0000:1b:00.0")
+        assert info["numa_node"] == 1
+        assert os.sched_getaffinity(0) == {allowed[0]}
+        assert info["bound"] == (len(before) > 1)
+        # Unknown slot: nothing changes.
+        info = bind_to_device_numa(sysfs=str(tmp_path), address="0000:99:00.0")
+        assert not info["bound"] and os.sched_getaffinity(0) == {allowed[0]}
+    finally:
+        os.sched_setaffinity(0, before)
