@@ -39,52 +39,6 @@ struct StageMeta {
     uint32_t layer, start, count, direct_mask, zero_mask, pad[3];
 };
 
-// Scale warps of the TMA variant: `lanes` threads starting at `lane_id`
-// gather the scales of every (layer, row) item, 4 items in flight per lane.
-__device__ __forceinline__ void gather_scales(const GatherParams &p, const uint64_t *s_sf, const uint32_t *s_entries,
-                                              const uint32_t *s_sfbase, uint32_t lane_id, uint32_t lanes) {
-    constexpr int kItems = 4;
-    const uint32_t total = p.layers * p.rows;
-    for (uint32_t base = lane_id; base < total; base += lanes * kItems) {
-        const float *src[kItems];
-        float *out[kItems];
-#pragma unroll
-        for (int u = 0; u < kItems; ++u) {
-            const uint32_t item = base + u * lanes;
-            src[u] = nullptr;
-            out[u] = nullptr;
-            if (item >= total)
-                continue;
-            // Items run in index order in both scale layouts, so the index
-            // reads coalesce (they cross PCIe when the indices sit in pinned
-            // host memory); column-major stores scatter 4 B each and merge in L2.
-            const uint32_t layer = item / p.rows;
-            const uint32_t r = item - layer * p.rows;
-            const uint32_t token = r / p.ept, slot = r - token * p.ept;
-            const int32_t x = __ldg(p.indices + item);
-            out[u] = p.sf_output + uint64_t(layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
-                     uint64_t(slot) * p.packs * p.sf_hidden_stride;
-            if (x >= 0) {
-                const uint32_t span = s_entries[layer] * p.sf_shard_div;
-                const uint32_t shard = uint32_t(x) / span;
-                if (shard < p.world && s_sf[shard] != 0)
-                    src[u] = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[layer] +
-                             uint64_t(uint32_t(x) - shard * span) * p.packs;
-            }
-        }
-        for (uint32_t k = 0; k < p.packs; ++k) {
-            float v[kItems];
-#pragma unroll
-            for (int u = 0; u < kItems; ++u)
-                v[u] = src[u] != nullptr ? __ldg(src[u] + k) : 0.0f;
-#pragma unroll
-            for (int u = 0; u < kItems; ++u)
-                if (out[u] != nullptr)
-                    out[u][uint64_t(k) * p.sf_hidden_stride] = v[u];
-        }
-    }
-}
-
 __device__ __forceinline__ void load_tables(const GatherParams &p, uint64_t *s_direct, uint64_t *s_sf,
                                             uint32_t *s_entries, uint32_t *s_tbase, uint32_t *s_sfbase) {
     for (uint32_t i = threadIdx.x; i < p.world; i += blockDim.x) {
@@ -111,12 +65,13 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + size_t(stages) * stage_bytes);
     uint64_t *empty = full + stages;
     StageMeta *meta = reinterpret_cast<StageMeta *>(empty + stages);
+    int32_t *stage_x = reinterpret_cast<int32_t *>(meta + stages);  // each stage's indices, for the scale warps
 
     load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < stages; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1);
+            mbar_init(empty + s, p.packs > 0 ? 2 : 1);  // consumer (+ the tile's scale warp)
         }
         fence_mbar_init();
     }
@@ -182,6 +137,8 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
             }
             const uint32_t direct_mask = __ballot_sync(0xFFFFFFFFu, src != nullptr);
             const uint32_t zero_mask = __ballot_sync(0xFFFFFFFFu, zero);
+            stage_x[stage * kBulkTile + lane] = x;
+            __syncwarp();  // the lanes' index stores precede lane 0's releasing arrive
             if (lane == 0) {
                 meta[stage] = StageMeta{layer, start, count, direct_mask, zero_mask, {0, 0, 0}};
                 mbar_arrive_expect_tx(full + stage, __popc(direct_mask) * p.row_bytes);
@@ -234,9 +191,49 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
                 mbar_arrive(empty + stage);
         }
     } else if (p.packs > 0) {
-        const uint32_t sf_warps = kBulkThreads / 32 - 2;
-        gather_scales(p, s_sf, s_entries, s_sfbase, blockIdx.x * sf_warps * 32 + (warp - 2) * 32 + lane,
-                      gridDim.x * sf_warps * 32);
+        // Scale warps: warp 2 + j takes the CTA's tiles k = j, j + 2, ...  It
+        // reads the tile's indices from the stage (never a second read from
+        // global or pinned host memory), copies each row's scales and then
+        // releases the stage together with the consumer.
+        constexpr uint32_t kSfWarps = kBulkThreads / 32 - 2;
+        const uint32_t j = warp - 2;
+        for (uint32_t t = t0 + j, k = j; t < t1; t += kSfWarps, k += kSfWarps) {
+            const uint32_t stage = k % stages, phase = k / stages;
+            if (!mbar_wait(full + stage, phase & 1, kPipelineTimeoutNs)) {
+                if (lane == 0)
+                    report_error(p.error, kPipelineTimeout, 0, 2 + j, t, 0);
+                break;
+            }
+            const StageMeta m = meta[stage];
+            const int32_t x = stage_x[stage * kBulkTile + lane];
+            __syncwarp();
+            if (lane < m.count) {
+                const uint32_t r = m.start + lane;
+                const uint32_t token = r / p.ept, slot = r - token * p.ept;
+                float *out = p.sf_output + uint64_t(m.layer) * p.sf_layer_stride + uint64_t(token) * p.sf_token_stride +
+                             uint64_t(slot) * p.packs * p.sf_hidden_stride;
+                const float *src = nullptr;
+                if (x >= 0) {
+                    const uint32_t span = s_entries[m.layer] * p.sf_shard_div;
+                    const uint32_t shard = uint32_t(x) / span;
+                    if (shard < p.world && s_sf[shard] != 0)
+                        src = reinterpret_cast<const float *>(s_sf[shard]) + s_sfbase[m.layer] +
+                              uint64_t(uint32_t(x) - shard * span) * p.packs;
+                }
+                uint32_t q = 0;
+                for (; q + 2 <= p.packs; q += 2) {
+                    const float v0 = src != nullptr ? __ldg(src + q) : 0.0f;
+                    const float v1 = src != nullptr ? __ldg(src + q + 1) : 0.0f;
+                    out[uint64_t(q) * p.sf_hidden_stride] = v0;
+                    out[uint64_t(q + 1) * p.sf_hidden_stride] = v1;
+                }
+                if (q < p.packs)
+                    out[uint64_t(q) * p.sf_hidden_stride] = src != nullptr ? __ldg(src + q) : 0.0f;
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(empty + stage);
+        }
     }
 }
 
@@ -418,7 +415,8 @@ cudaError_t launch_bulk(const GatherParams &p, int num_sms, cudaStream_t stream)
     const uint32_t stage_bytes = kBulkTile * p.row_bytes;
     uint32_t stages = kStageTargetBytes / stage_bytes;
     stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
-    const size_t smem = size_t(stages) * stage_bytes + size_t(stages) * (16 + sizeof(StageMeta));
+    const size_t smem =
+        size_t(stages) * stage_bytes + size_t(stages) * (16 + sizeof(StageMeta) + kBulkTile * sizeof(int32_t));
     static size_t configured = 0;
     if (smem > configured) {
         cudaError_t rc =
