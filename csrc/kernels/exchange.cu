@@ -229,10 +229,13 @@ __global__ void __launch_bounds__(kPushThreads) hook_kernel(const __grid_constan
     __shared__ uint64_t s_task;
     const ServeParams &s = p.s;
     const uint64_t start = global_timer_ns();
+    const uint64_t max_polls = p.timeout_ns / 16 + 1024;  // holds even if the timer stalled
+    uint64_t polls = 0;
     uint32_t backoff = 64;
     while (true) {
         if (threadIdx.x == 0) {
             int32_t state = 1;  // 1: all done, 0: waiting, 2: timed out
+            ++polls;
             for (uint32_t o = 0; o < s.world; ++o) {
                 const uint32_t slot = p.layer * s.world + o;
                 if (p.totals[slot] == 0)
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kPushThreads) hook_kernel(const __grid_constan
                 const uint64_t seen = ld_acquire_sys_u64(p.done + slot);
                 if (seen != expected) {
                     state = 0;
-                    if (global_timer_ns() - start > p.timeout_ns) {
+                    if (global_timer_ns() - start > p.timeout_ns || polls > max_polls) {
                         report_error(s.error, kWaitTimeout, p.layer, o, seen, expected);
                         state = 2;
                     }

@@ -193,4 +193,38 @@ cudaError_t launch_expand(const DedupParams &p, int num_sms, cudaStream_t stream
 cudaError_t launch_wait_probe(const uint64_t *flag, uint64_t expected, uint64_t timeout_ns, ErrorSink error,
                               cudaStream_t stream);
 
+// Message-passing litmus test of the release/acquire flag protocol.
+enum LitmusRole : uint32_t { kLitmusProducer = 0, kLitmusConsumer = 1, kLitmusBoth = 2 };
+enum LitmusStatus : uint32_t { kLitmusProducerTimeout = 1, kLitmusConsumerTimeout = 2 };
+
+struct LitmusResult {
+    uint32_t status;           // 0, or the LitmusStatus of the side that gave up first
+    uint32_t epoch;            // epoch of that wait
+    uint32_t mismatches;       // words that differed from the acquired epoch's values
+    uint32_t first_bad_epoch;  // 0xFFFFFFFF when none
+    uint32_t epochs_done;      // last epoch the consumer acknowledged
+    uint32_t pad;
+    uint64_t observed;         // flag value seen when the wait gave up
+};
+
+struct LitmusParams {
+    uint32_t *data_remote;       // producer: data in the consumer's memory
+    const uint32_t *data_local;  // consumer: the same data, local
+    uint64_t *flag_remote;       // producer releases epochs here (consumer's memory)
+    const uint64_t *flag_local;  // consumer polls
+    uint64_t *ack_remote;        // consumer acknowledges here (producer's memory)
+    const uint64_t *ack_local;   // producer polls
+    uint32_t *prod_count;        // arrivals of this GPU's producer CTAs
+    uint32_t *cons_count;        // arrivals of this GPU's consumer CTAs
+    LitmusResult *result;
+    uint32_t words;  // per epoch, a multiple of 4
+    uint32_t epochs;
+    uint32_t role;   // LitmusRole
+    uint32_t weak_loads;
+    uint64_t timeout_ns;
+};
+
+// Cooperative launch of `ctas` CTAs per role (2 x ctas for kLitmusBoth).
+cudaError_t launch_litmus(const LitmusParams &p, uint32_t ctas, cudaStream_t stream);
+
 } // namespace engram

@@ -38,6 +38,16 @@ __device__ __forceinline__ Vec16 ld_v4(const void *ptr) {
     return v;
 }
 
+// 16-byte load cached in L2 only: never a stale L1 line of memory that a peer
+// rewrites while this kernel runs.
+__device__ __forceinline__ Vec16 ld_cg_v4(const void *ptr) {
+    Vec16 v;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr));
+    return v;
+}
+
 __device__ __forceinline__ void st_v4(void *ptr, const Vec16 &v) {
     asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
@@ -146,13 +156,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for a barrier phase; false after `timeout_ns`.
+// Bounded wait for a barrier phase; false after `timeout_ns` (or as many
+// polls, a cap that holds even if the timer stalled).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity))
         return true;
     const uint64_t start = global_timer_ns();
+    uint64_t polls = 0;
     while (!mbar_try_wait(bar, parity))
-        if (global_timer_ns() - start > timeout_ns)
+        if (global_timer_ns() - start > timeout_ns || ++polls > timeout_ns)
             return false;
     return true;
 }
@@ -202,14 +214,18 @@ __device__ __forceinline__ bool dedup_duplicate(const GatherParams &p, uint32_t 
 }
 
 // Poll `flag` until it equals `expected` or `timeout_ns` passes.  Returns the
-// last value read.  Never traps; the caller reports a timeout.
+// last value read.  Never traps; the caller reports a timeout.  An iteration
+// cap (each poll sleeps at least ~8 ns) bounds the loop even if the timer
+// stalled.
 __device__ __forceinline__ uint64_t wait_flag_eq(const void *flag, uint64_t expected, uint64_t timeout_ns,
                                                  bool *timed_out) {
     const uint64_t start = global_timer_ns();
+    const uint64_t max_polls = timeout_ns / 8 + 1024;
+    uint64_t polls = 0;
     uint32_t backoff = 32;
     uint64_t value = ld_acquire_sys_u64(flag);
     while (value != expected) {
-        if (global_timer_ns() - start > timeout_ns) {
+        if (global_timer_ns() - start > timeout_ns || ++polls > max_polls) {
             *timed_out = true;
             return value;
         }

@@ -606,6 +606,92 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         return double(ms) * 1e3;
     }
 
+    // Litmus test of the release/acquire flag protocol (between fetches only;
+    // it overwrites the output region).  Header words sit at the start of
+    // each rank's output region, the data after 4 KiB.  reset() zeroes this
+    // rank's header; call it on both ranks and barrier before run().
+    static constexpr size_t kLitmusData = 4096;
+    void debug_litmus_reset() {
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaMemset(reinterpret_cast<void *>(arena_->ptr() + dev_output_), 0, kLitmusData), "litmus reset");
+        check_cuda(cudaDeviceSynchronize(), "litmus reset sync");
+    }
+
+    py::dict debug_litmus(uint32_t peer, const std::string &role, uint32_t epochs, uint32_t words, uint32_t ctas,
+                          bool weak_loads, double timeout_ms) {
+        check(connected_ && peer < world_ && (peer == rank_ || peer_dev_[peer]), "peer not mapped");
+        const size_t region = size_t(layers_) * capacity_ * row_bytes_;
+        words = words / 4 * 4;
+        check(words > 0 && kLitmusData + size_t(words) * 4 <= region, "litmus data exceeds the output region");
+        check(ctas >= 1 && ctas <= 256, "litmus ctas out of range");
+        LitmusParams lp{};
+        if (role == "producer")
+            lp.role = kLitmusProducer;
+        else if (role == "consumer")
+            lp.role = kLitmusConsumer;
+        else if (role == "both")
+            lp.role = kLitmusBoth;
+        else
+            check(false, "litmus role must be producer, consumer or both");
+        check((lp.role == kLitmusBoth) == (peer == rank_), "role 'both' runs on this GPU alone");
+        c10::cuda::CUDAGuard guard(device_);
+        uint8_t *mine = reinterpret_cast<uint8_t *>(arena_->ptr() + dev_output_);
+        uint8_t *theirs =
+            reinterpret_cast<uint8_t *>((peer == rank_ ? arena_->ptr() : peer_dev_[peer]->ptr()) + dev_output_);
+        // Producer writes data and flag into the consumer's region; the
+        // consumer acknowledges into the producer's region.
+        uint8_t *consumer_base = lp.role == kLitmusConsumer ? mine : theirs;
+        uint8_t *producer_base = lp.role == kLitmusConsumer ? theirs : mine;
+        lp.data_remote = reinterpret_cast<uint32_t *>(consumer_base + kLitmusData);
+        lp.data_local = reinterpret_cast<const uint32_t *>(mine + kLitmusData);
+        lp.flag_remote = reinterpret_cast<uint64_t *>(consumer_base);
+        lp.flag_local = reinterpret_cast<const uint64_t *>(mine);
+        lp.ack_remote = reinterpret_cast<uint64_t *>(producer_base + 64);
+        lp.ack_local = reinterpret_cast<const uint64_t *>(mine + 64);
+        lp.prod_count = reinterpret_cast<uint32_t *>(mine + 128);
+        lp.cons_count = reinterpret_cast<uint32_t *>(mine + 192);
+        lp.words = words;
+        lp.epochs = epochs;
+        lp.weak_loads = weak_loads ? 1 : 0;
+        lp.timeout_ns = uint64_t(timeout_ms * 1e6);
+        LitmusResult init{};
+        init.first_bad_epoch = 0xFFFFFFFFu;
+        LitmusResult *result = nullptr;
+        check_cuda(cudaMalloc(&result, sizeof(LitmusResult)), "litmus result");
+        lp.result = result;
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        LitmusResult out{};
+        cudaError_t rc = cudaMemcpyAsync(result, &init, sizeof(init), cudaMemcpyHostToDevice, s);
+        if (rc == cudaSuccess) {
+            cudaEventRecord(a, s);
+            rc = launch_litmus(lp, ctas, s);
+            cudaEventRecord(b, s);
+        }
+        if (rc == cudaSuccess)
+            rc = cudaMemcpyAsync(&out, result, sizeof(out), cudaMemcpyDeviceToHost, s);
+        if (rc == cudaSuccess)
+            rc = cudaStreamSynchronize(s);
+        float ms = 0;
+        if (rc == cudaSuccess)
+            cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        cudaFree(result);
+        check_cuda(rc, "litmus run");
+        py::dict d;
+        d["status"] = out.status;
+        d["epoch"] = out.epoch;
+        d["observed"] = out.observed;
+        d["mismatches"] = out.mismatches;
+        d["first_bad_epoch"] = out.first_bad_epoch == 0xFFFFFFFFu ? -1 : int64_t(out.first_bad_epoch);
+        d["epochs_done"] = out.epochs_done;
+        d["ms"] = double(ms);
+        return d;
+    }
+
     // Fault injection for tests: stop serving requesters, as a dead owner
     // process would.  Requesters then see their bounded hook wait run out.
     void debug_stop_service() {
@@ -1117,6 +1203,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("run_wait_probe", &Runtime::run_wait_probe)
         .def("debug_stop_service", &Runtime::debug_stop_service)
         .def("debug_peer_copy", &Runtime::debug_peer_copy)
+        .def("debug_litmus_reset", &Runtime::debug_litmus_reset)
+        .def("debug_litmus", &Runtime::debug_litmus, py::arg("peer"), py::arg("role"), py::arg("epochs"),
+             py::arg("words"), py::arg("ctas") = 32, py::arg("weak_loads") = false, py::arg("timeout_ms") = 2000.0)
         .def("close", &Runtime::close)
         .def_property_readonly("closed", &Runtime::closed);
     py::class_<OwnerServiceHarness>(m, "OwnerServiceHarness")

@@ -252,6 +252,35 @@ def _dead_owner_times_out(rank, world):
     buf.destroy()
 
 
+def _litmus(rank, world):
+    _setup(rank)
+    buf = _buffer((4099, 4111), 256, 512, 24, torch.bfloat16, 0, egm=True)
+    rt = buf.runtime
+    for producer, words, epochs, weak in ((0, 64, 4000, False), (1, 65536, 1000, False), (0, 4096, 2000, True)):
+        consumer = 1 - producer
+        rt.debug_litmus_reset()
+        dist.barrier()
+        if rank == producer:
+            r = rt.debug_litmus(consumer, "producer", epochs, words, ctas=16, weak_loads=weak, timeout_ms=5000.0)
+            assert r["status"] == 0, r
+        elif rank == consumer:
+            r = rt.debug_litmus(producer, "consumer", epochs, words, ctas=16, weak_loads=weak, timeout_ms=5000.0)
+            assert r["status"] == 0 and r["mismatches"] == 0 and r["epochs_done"] == epochs, r
+        dist.barrier()
+    # A consumer whose producer never runs gives up after its bounded wait.
+    rt.debug_litmus_reset()
+    dist.barrier()
+    if rank == 1:
+        r = rt.debug_litmus(0, "consumer", 10, 64, ctas=2, timeout_ms=200.0)
+        assert r["status"] == 2 and r["epoch"] == 1 and r["epochs_done"] == 0, r
+    dist.barrier()
+    buf.destroy()
+
+
+def test_flag_protocol_litmus_two_gpus(port):
+    run_ranks(_litmus, 2, port)
+
+
 def test_peer_hbm_route(port):
     run_ranks(_peer_hbm, _world(), port)
 

@@ -304,3 +304,21 @@ def test_pinned_host_indices_under_graph_capture():
         del graph
     finally:
         buf.destroy()
+
+
+@pytest.mark.parametrize("weak_loads", [False, True])
+def test_flag_protocol_litmus_one_gpu(weak_loads):
+    """Producer and consumer CTAs of one cooperative launch run the release/acquire protocol for many epochs."""
+    buf = make_buffer((4099, 4111), 256, 512, 24, torch.bfloat16, 0, True)
+    try:
+        rt = buf.runtime
+        for words, epochs in ((64, 4000), (65536, 1000)):
+            rt.debug_litmus_reset()
+            r = rt.debug_litmus(0, "both", epochs, words, ctas=16, weak_loads=weak_loads, timeout_ms=2000.0)
+            assert r["status"] == 0, r
+            assert r["mismatches"] == 0 and r["first_bad_epoch"] == -1, r
+            assert r["epochs_done"] == epochs, r
+        with pytest.raises(RuntimeError, match="alone"):
+            rt.debug_litmus(0, "producer", 1, 64)
+    finally:
+        buf.destroy()
