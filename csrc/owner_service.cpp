@@ -1,4 +1,5 @@
 #include "owner_service.h"
+#include "trace.h"
 
 #include <chrono>
 #include <cstdio>
@@ -97,7 +98,10 @@ void OwnerService::loop() {
                 requests_.fetch_add(batch.size(), std::memory_order_relaxed);
                 batches_.fetch_add(1, std::memory_order_relaxed);
                 const auto t0 = std::chrono::steady_clock::now();
-                launcher_(batch);
+                {
+                    TraceRange trace("engram/owner_push");
+                    launcher_(batch);
+                }
                 last_work = std::chrono::steady_clock::now();
                 const uint64_t us = uint64_t(
                     std::chrono::duration_cast<std::chrono::microseconds>(last_work - t0).count());

@@ -38,6 +38,7 @@
 #include "kernels/params.h"
 #include "memory.h"
 #include "owner_service.h"
+#include "trace.h"
 
 namespace py = pybind11;
 
@@ -109,6 +110,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         check(at < (1ull << 32) && sf_at < (1ull << 32), "local vocabulary too large");
         table_rows_ = at;
 
+        if (cfg.contains("nvtx") && get<bool>(cfg, "nvtx"))
+            nvtx_enabled().store(true);
         py::dict plan = get<py::dict>(cfg, "plan");
         auto off = [&](const char *k) { return get<size_t>(plan, k); };
         dev_mirror_ = off("dev_mirror");
@@ -283,6 +286,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
 
     // ------------------------------------------------------------------ write
     void write(uint32_t layer, const torch::Tensor &storage, const c10::optional<torch::Tensor> &scales) {
+        TraceRange trace("engram/write");
         check_health();
         check(ready_ && !closed_, "runtime not ready");
         check(layer < layers_, "write layer out of range");
@@ -348,6 +352,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     }
 
     py::list fetch(const torch::Tensor &indices, uint32_t channels, bool col_major) {
+        TraceRange trace("engram/fetch");
         check_health();
         check(connected_ && !closed_, "runtime is not connected");
         check(indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_contiguous() &&
@@ -422,6 +427,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     }
 
     void wait_layer(uint32_t layer) {
+        TraceRange trace("engram/hook");
         check_health();
         check(connected_ && !closed_, "runtime is not connected");
         check(layer < layers_, "hook layer out of range");
@@ -1222,6 +1228,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("stop", &FdServer::stop)
         .def_property_readonly("served", &FdServer::served);
     m.def("fetch_fd", &fetch_fd, py::arg("name"), py::arg("index"), py::arg("timeout_s") = 30.0);
+    m.def("set_nvtx", [](bool on) { nvtx_enabled().store(on); }, py::arg("enabled"),
+          "Enable NVTX ranges around fetch, hook, write and owner-service launches.");
+    m.def("nvtx_enabled", []() { return nvtx_enabled().load(); });
     m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),
           py::arg("packed"), py::arg("counts"), py::arg("scratch"));
     m.def("memfd_with_bytes", &memfd_with_bytes);

@@ -105,3 +105,18 @@ def _fd_exchange(rank, world, token):
 
 def test_fd_exchange_across_processes(port):
     run_ranks(_fd_exchange, 3, port, args=(str(port),))
+
+
+def test_nvtx_ranges_toggle_and_run_without_a_profiler():
+    assert C.nvtx_enabled() is False
+    C.set_nvtx(True)
+    try:
+        assert C.nvtx_enabled() is True
+        h = C.OwnerServiceHarness(2, 1, 64, [0, 1])  # launches run inside an NVTX range
+        h.start()
+        h.publish(1, 0, 1, 5, 1)
+        assert _wait(lambda: len(h.launched()) == 1)
+        h.stop()
+        assert h.error() == ""
+    finally:
+        C.set_nvtx(False)
