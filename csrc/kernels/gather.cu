@@ -33,7 +33,7 @@ constexpr int kBulkThreads = 128;       // producer warp, consumer warp, 2 scale
 constexpr uint32_t kStageTargetBytes = 64 * 1024;
 constexpr uint64_t kPipelineTimeoutNs = 2000000000ull;
 constexpr uint32_t kIndexDepth = 8;     // tiles of indices in flight per producer
-constexpr uint32_t kIndexAhead = 4;     // SIMT: groups of indices in flight per warp
+constexpr uint32_t kIndexAhead = 4;     // SIMT: steps of indices in flight per warp
 
 struct StageMeta {
     uint32_t layer, start, count, direct_mask, zero_mask, pad[3];
@@ -238,11 +238,11 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 }
 
 // ------------------------------------------------------------ SIMT variant
-// A warp owns groups of 32 consecutive (layer, row) items.  Lane l resolves
+// A warp walks its items 32 at a time (one step).  Lane l resolves the step's
 // item l once (owner, source, destination, scales) and the copy loop hands the
 // 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
 // per-row integer work is done by one lane instead of LPR lanes.  The next
-// kIndexAhead groups' indices are loaded before this group's rows, hiding that latency.
+// kIndexAhead steps' indices are loaded before this step's rows, hiding that latency.
 template <int LPR, int VPL, int UNROLL>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
@@ -257,31 +257,48 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     const uint32_t sub = lane / LPR, vlane = lane % LPR;
     const uint32_t vectors = p.row_bytes / 16;
     const uint32_t total = p.layers * p.rows;
-    const uint32_t groups = (total + 31) / 32;
     const uint32_t warp_id = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const uint32_t warp_stride = gridDim.x * (blockDim.x / 32);
+    const uint32_t warps = gridDim.x * (blockDim.x / 32);
+    // Work split.  Contiguous (default): warp w owns items [lo, hi), an equal
+    // share of all items, so no warp runs a whole 32-row group more than
+    // another (with 4736 warps and 6144 groups, a group stride leaves some
+    // warps two groups and others one).  Strided: warp w owns groups
+    // w, w + warps, ...  Step k covers items base(k) + lane.
+    uint32_t lo, hi, step_stride, steps;
+    if (p.strided) {
+        lo = warp_id * 32;
+        hi = total;
+        step_stride = warps * 32;
+        steps = lo < total ? (total - lo + step_stride - 1) / step_stride : 0;
+    } else {
+        const uint32_t share = (total + warps - 1) / warps;
+        lo = min(warp_id * share, total);
+        hi = min(lo + share, total);
+        step_stride = 32;
+        steps = (hi - lo + 31) / 32;
+    }
 
     const uint32_t epoch = p.dedup ? dedup_epoch(p.dedup_state) : 0;
-    // The indices of this warp's next kIndexAhead groups are in flight at
+    // The indices of this warp's next kIndexAhead steps are in flight at
     // once, copied by cp.async into a per-warp shared ring.  Their completion
     // is tracked apart from the row loads' registers, so a row copy never
-    // waits on a later group's index (a PCIe round trip when the indices sit
+    // waits on a later step's index (a PCIe round trip when the indices sit
     // in pinned host memory).  Each lane reads back only what it copied.
     int32_t *ring = s_index[threadIdx.x / 32];
 #pragma unroll
     for (uint32_t a = 0; a < kIndexAhead; ++a) {
-        const uint32_t ga = warp_id + a * warp_stride;
-        const uint32_t item = ga * 32 + lane;
-        if (ga < groups && item < total)
+        const uint32_t item = lo + a * step_stride + lane;
+        if (a < steps && item < hi)
             cp_async_4(ring + a * 32 + lane, p.indices + item);
         else
             *reinterpret_cast<volatile int32_t *>(ring + a * 32 + lane) = -1;
         cp_async_commit();
     }
-    uint32_t k = 0;
-    for (uint32_t g = warp_id; g < groups; g += warp_stride, ++k) {
-        const uint32_t item = g * 32 + lane;
-        cp_async_wait<kIndexAhead - 1>();  // group k has landed
+    for (uint32_t k = 0; k < steps; ++k) {
+        const uint32_t base = lo + k * step_stride;
+        const uint32_t item = base + lane;
+        const uint32_t live = min(32u, hi - base);  // items of this step
+        cp_async_wait<kIndexAhead - 1>();  // step k has landed
         int32_t *slot_x = ring + (k % kIndexAhead) * 32 + lane;
         const int32_t x = *reinterpret_cast<volatile int32_t *>(slot_x);
         // Resolve this lane's item; its scale loads are issued now and stored
@@ -290,7 +307,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
         float *sf_out = nullptr;
         const float *sf_src = nullptr;
         float sf_val[kMaxPacksInFlight];
-        if (item < total) {
+        if (item < hi) {
             const uint32_t layer = item / p.rows;
             const uint32_t at = item - layer * p.rows;
             dst = reinterpret_cast<uint64_t>(p.output) + (uint64_t(layer) * p.capacity + at) * p.row_bytes;
@@ -324,24 +341,26 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                     sf_val[k] = (sf_src != nullptr && k < p.packs) ? __ldg(sf_src + k) : 0.0f;
             }
         }
-        // Refill the slot with group k + kIndexAhead (x is consumed above).
+        // Refill the slot with step k + kIndexAhead (x is consumed above).
         {
-            const uint32_t g_next = g + kIndexAhead * warp_stride;
-            const uint32_t nitem = g_next * 32 + lane;
-            if (g_next < groups && nitem < total)
+            const uint32_t next = k + kIndexAhead;
+            const uint32_t nitem = lo + next * step_stride + lane;
+            if (next < steps && nitem < hi)
                 cp_async_4(slot_x, p.indices + nitem);
             else
                 *reinterpret_cast<volatile int32_t *>(slot_x) = -1;
             cp_async_commit();
         }
-        // Copy the group's rows: UNROLL row-steps x VPL vectors in flight per lane.
-        for (uint32_t r0 = 0; r0 < 32; r0 += kRowsPerStep * UNROLL) {
+        // Copy the step's rows: UNROLL row-steps x VPL vectors in flight per lane.
+        for (uint32_t r0 = 0; r0 < live; r0 += kRowsPerStep * UNROLL) {
             uint64_t rs[UNROLL], rd[UNROLL];
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
                 const uint32_t r = r0 + u * kRowsPerStep + sub;
-                rs[u] = __shfl_sync(0xFFFFFFFFu, src, r);
-                rd[u] = __shfl_sync(0xFFFFFFFFu, dst, r);
+                rs[u] = __shfl_sync(0xFFFFFFFFu, src, r % 32);
+                rd[u] = __shfl_sync(0xFFFFFFFFu, dst, r % 32);
+                if (r >= live)  // past this step's items (and no lane-wrapped repeats)
+                    rs[u] = rd[u] = 0;
             }
             for (uint32_t chunk = 0; chunk < vectors; chunk += LPR * VPL) {
                 Vec16 buf[UNROLL][VPL];

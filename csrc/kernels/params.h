@@ -85,6 +85,7 @@ struct GatherParams {
     uint32_t variant;             // kGatherBulk or kGatherSimt
     uint32_t ctas_per_sm;         // SIMT grid cap per SM (0 = default 2)
     uint32_t unroll;              // SIMT row-steps in flight for 256-byte rows (0 = default)
+    uint32_t strided;             // SIMT: 1 = warps stride over 32-row groups, 0 = equal contiguous ranges
     // Request deduplication (see DedupParams): when `dedup` is set, an item whose
     // slot's elected first occurrence is another item is skipped here and
     // copied locally by the expand kernel afterwards.

@@ -90,6 +90,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         tuning_ctas_per_sm_ = get<uint32_t>(cfg, "gather_ctas_per_sm");
         dedup_mode_ = get<int>(cfg, "dedup");
         tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
+        if (cfg.contains("gather_strided"))
+            tuning_strided_ = get<uint32_t>(cfg, "gather_strided");
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
         capacity_ = max_tokens_ * ept_;
@@ -829,6 +831,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         dedup_slots_ = slots;
         g.ctas_per_sm = tuning_ctas_per_sm_;
         g.unroll = tuning_unroll_;
+        g.strided = tuning_strided_;
 
         DispatchParams &d = dispatch_;
         d = DispatchParams{};
@@ -956,7 +959,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint32_t row_bytes_ = 0, capacity_ = 0;
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
-    uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0;
+    uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0, tuning_strided_ = 0;
     std::string gather_choice_ = "auto";
     // request deduplication: mode 0 off, 1 on, 2 auto (on while the last
     // measured unique ratio is below kDedupOnRatio; re-measured every

@@ -217,6 +217,7 @@ class EngramBuffer(EngramBufferBase):
             gather_kernel=_gather_kernel(),
             gather_ctas_per_sm=env_int("ENGRAM_GATHER_CTAS_PER_SM", 0, minimum=0),
             gather_unroll=env_int("ENGRAM_GATHER_UNROLL", 0, minimum=0),
+            gather_strided=env_int("ENGRAM_GATHER_STRIDED", 0, minimum=0),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
         )
