@@ -231,7 +231,7 @@ def main():
             "scaling": "weak",
             "vs_baseline": round(per_req_gbs / BASELINE_GBS_PER_REQUESTER, 3),
             "dtype": "fp8_e4m3" if spec.num_sf_packs else "bf16",
-            "data": "synthetic (random-init tables, seeded uniform indices)",
+            "data": f"synthetic (random-init tables, seeded {spec.distribution} indices)",
             "impl": "ours" if native else "nccl_all_to_all_baseline",
             "per_requester_gbs": round(per_req_gbs, 3),
             "p50_fetch_to_hook_us": round(statistics.median(per_step_max) * 1e3, 2),
@@ -250,6 +250,7 @@ def main():
                 "bytes_per_requester_per_step": bytes_req,
                 "parallelism": f"vocab-sharded x{world} (every rank requester and owner)",
                 "numa": NUMA,
+                "hot_rows": getattr(buf, "hot_rows", None),
                 "route": args.route if native else "all_to_all",
                 "graph": bool(args.graph),
                 "distribution": spec.distribution,

@@ -62,7 +62,8 @@ __global__ void __launch_bounds__(kDedupThreads) dedup_kernel(const __grid_const
             const int32_t x = __ldg(p.indices + item);
             if (x >= 0) {
                 const uint32_t owner = uint32_t(x) / p.layer.entries[layer];
-                if (owner < p.world && p.direct_base[owner] != 0)
+                // Replicated hot rows are local reads: nothing to save.
+                if (owner < p.world && p.direct_base[owner] != 0 && uint32_t(x) >= p.layer.hot_rows[layer])
                     key = (uint64_t(epoch) << 36) | (uint64_t(layer) << 31) | uint32_t(x);
             }
         }

@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid
     const uint32_t layer = blockIdx.y;
     const uint32_t n = p.layer.entries[layer];
     const uint32_t tbase = p.layer.table_bases[layer];
+    const uint32_t hot = p.layer.hot_rows[layer];
     const uint32_t lo = blockIdx.x * p.tile_rows;
     const uint32_t hi = min(lo + p.tile_rows, p.rows);
     const uint32_t lane = threadIdx.x % 32;
@@ -52,7 +53,8 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid
                 owner = p.world;
             }
         }
-        const bool host = owner < p.world && p.inbox_base[owner] != 0;
+        // Replicated hot rows are read locally by the gather, never pushed.
+        const bool host = owner < p.world && p.inbox_base[owner] != 0 && uint32_t(x) >= hot;
         const uint32_t key = host ? owner : 0xFFFFFFFFu;
         const uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
         if (host) {

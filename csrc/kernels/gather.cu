@@ -40,7 +40,8 @@ struct StageMeta {
 };
 
 __device__ __forceinline__ void load_tables(const GatherParams &p, uint64_t *s_direct, uint64_t *s_sf,
-                                            uint32_t *s_entries, uint32_t *s_tbase, uint32_t *s_sfbase) {
+                                            uint32_t *s_entries, uint32_t *s_tbase, uint32_t *s_sfbase,
+                                            uint32_t *s_hot, uint32_t *s_hotbase) {
     for (uint32_t i = threadIdx.x; i < p.world; i += blockDim.x) {
         s_direct[i] = p.direct_base[i];
         s_sf[i] = p.sf_base[i];
@@ -49,6 +50,8 @@ __device__ __forceinline__ void load_tables(const GatherParams &p, uint64_t *s_d
         s_entries[i] = p.layer.entries[i];
         s_tbase[i] = p.layer.table_bases[i];
         s_sfbase[i] = p.layer.sf_bases[i];
+        s_hot[i] = p.layer.hot_rows[i];
+        s_hotbase[i] = p.layer.hot_bases[i];
     }
 }
 
@@ -59,6 +62,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
+    __shared__ uint32_t s_hot[kMaxLayers], s_hotbase[kMaxLayers];
     __shared__ int32_t s_index[kIndexDepth * kBulkTile];
     const uint32_t stage_bytes = kBulkTile * p.row_bytes;
     uint8_t *data = smem;
@@ -67,7 +71,7 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
     StageMeta *meta = reinterpret_cast<StageMeta *>(empty + stages);
     int32_t *stage_x = reinterpret_cast<int32_t *>(meta + stages);  // each stage's indices, for the scale warps
 
-    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
+    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase, s_hot, s_hotbase);
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < stages; ++s) {
             mbar_init(full + s, 1);
@@ -128,6 +132,9 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
                     if (owner >= p.world) {
                         zero = true;
                         report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
+                    } else if (uint32_t(x) < s_hot[layer]) {
+                        src = reinterpret_cast<const uint8_t *>(p.hot_base) +
+                              (uint64_t(s_hotbase[layer]) + uint32_t(x)) * p.row_bytes;
                     } else if (s_direct[owner] != 0 &&
                                !(p.dedup && dedup_duplicate(p, layer * p.rows + start + lane, epoch))) {
                         const uint64_t row = uint64_t(s_tbase[layer]) + (uint32_t(x) - owner * n);
@@ -248,7 +255,8 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ int32_t s_index[kSimtThreads / 32][kIndexAhead * 32];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
-    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase);
+    __shared__ uint32_t s_hot[kMaxLayers], s_hotbase[kMaxLayers];
+    load_tables(p, s_direct, s_sf, s_entries, s_tbase, s_sfbase, s_hot, s_hotbase);
     __syncthreads();
 
     constexpr uint32_t kRowsPerStep = 32 / LPR;
@@ -316,6 +324,8 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                 const uint32_t owner = uint32_t(x) / n;
                 if (owner >= p.world) {
                     report_error(p.error, kIndexOutOfRange, layer, owner, uint64_t(x), 0);
+                } else if (uint32_t(x) < s_hot[layer]) {  // replicated hot row: local copy
+                    src = p.hot_base + (uint64_t(s_hotbase[layer]) + uint32_t(x)) * p.row_bytes;
                 } else if (s_direct[owner] != 0) {
                     if (p.dedup && dedup_duplicate(p, item, epoch))
                         dst = 0;  // a repeat: copied from its first occurrence after the gather

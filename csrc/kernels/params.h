@@ -63,6 +63,10 @@ struct LayerTable {
     uint32_t entries[kMaxLayers];      // rows per rank (n_l)
     uint32_t table_bases[kMaxLayers];  // first local row of layer l in a shard
     uint32_t sf_bases[kMaxLayers];     // first float of layer l in a scale table
+    // Hot-prefix replication: global ids [0, hot_rows[l]) of layer l are read
+    // from this rank's replica (row hot_bases[l] + x), never from their owner.
+    uint32_t hot_rows[kMaxLayers];
+    uint32_t hot_bases[kMaxLayers];
 };
 
 // Requester-side gather: every row whose owner has a direct source (the
@@ -76,6 +80,7 @@ struct GatherParams {
     LayerTable layer;
     uint64_t direct_base[kMaxRanks];  // per owner; 0 = rows arrive by owner push
     uint64_t sf_base[kMaxRanks];      // per scale shard
+    uint64_t hot_base;                // local replica of the hot prefixes (LayerTable::hot_rows)
     uint32_t layers, rows, tokens, ept;
     uint32_t capacity, row_bytes, world, packs;
     uint32_t sf_shard_div;        // global row -> shard: x / (n * sf_shard_div)

@@ -73,10 +73,16 @@ void OwnerService::loop() {
                     uint64_t &done = completed_[size_t(r) * c.layers + l];
                     if (epoch == done)
                         continue;
-                    if (epoch != done + 1)
-                        throw std::runtime_error("mailbox sequence skipped: requester " + std::to_string(r) +
+                    // A jump forward is legal: the owner's hook kernels serve
+                    // requests too, and a requester publishes a layer's next
+                    // epoch only after every owner released the previous one,
+                    // so the epochs in between are complete.  Going back is not.
+                    if (epoch < done)
+                        throw std::runtime_error("mailbox sequence went backwards: requester " + std::to_string(r) +
                                                  " layer " + std::to_string(l) + " epoch " + std::to_string(epoch) +
                                                  " after " + std::to_string(done));
+                    if (epoch > done + 1)
+                        skipped_.fetch_add(epoch - done - 1, std::memory_order_relaxed);
                     const uint32_t rows = __atomic_load_n(&h->rows, __ATOMIC_RELAXED);
                     const uint32_t layer = __atomic_load_n(&h->layer, __ATOMIC_RELAXED);
                     const uint32_t requester = __atomic_load_n(&h->requester, __ATOMIC_RELAXED);

@@ -48,6 +48,8 @@ class OwnerService {
     uint64_t requests() const { return requests_.load(); }
     uint64_t rows() const { return rows_.load(); }
     uint64_t batches() const { return batches_.load(); }
+    // Epochs the owner's hook kernels finished before this thread saw them.
+    uint64_t skipped() const { return skipped_.load(); }
     // Longest time one launcher call took (host side), in microseconds.
     uint64_t max_launch_us() const { return max_launch_us_.load(); }
     // Epoch this service last accepted from (requester, layer).
@@ -62,7 +64,7 @@ class OwnerService {
     std::function<void()> thread_init_;
     std::vector<uint64_t> completed_;
     std::atomic<bool> stop_{false};
-    std::atomic<uint64_t> requests_{0}, rows_{0}, batches_{0}, max_launch_us_{0};
+    std::atomic<uint64_t> requests_{0}, rows_{0}, batches_{0}, max_launch_us_{0}, skipped_{0};
     std::mutex error_mutex_;
     std::string error_;
     std::thread thread_;

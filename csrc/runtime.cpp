@@ -125,6 +125,22 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         dev_inbox_ = off("dev_inbox");
         dev_dedup_ = off("dev_dedup");
         dev_dedup_bytes_ = off("dev_dedup_bytes");
+        dev_replica_ = off("dev_replica");
+        dev_replica_bytes_ = off("dev_replica_bytes");
+        hot_rows_.assign(layers_, 0);
+        hot_bases_.assign(layers_, 0);
+        if (cfg.contains("hot_rows")) {
+            const auto hot = get<std::vector<uint32_t>>(cfg, "hot_rows");
+            check(hot.size() == layers_, "hot_rows needs one count per layer");
+            uint64_t at = 0;
+            for (uint32_t l = 0; l < layers_; ++l) {
+                check(uint64_t(hot[l]) <= uint64_t(entries_[l]) * world_, "hot_rows exceeds the layer's global rows");
+                hot_rows_[l] = hot[l];
+                hot_bases_[l] = uint32_t(at);
+                at += hot[l];
+            }
+            check(at * row_bytes_ == dev_replica_bytes_, "replica region does not match hot_rows");
+        }
         dev_scratch_ = off("dev_scratch");
         dev_scratch_bytes_ = off("dev_scratch_bytes");
         device_bytes_ = off("device_bytes");
@@ -497,6 +513,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["served_requests"] = service_.requests();
         d["served_rows"] = service_.rows();
         d["push_batches"] = service_.batches();
+        d["epochs_served_by_hooks_unseen"] = service_.skipped();
         d["max_push_launch_us"] = service_.max_launch_us();
         d["egm_enabled"] = egm_;
         bool direct_remote = false;
@@ -521,7 +538,33 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
         d["dedup_fetches"] = dedup_fetches_;
         d["dedup_last_unique_ratio"] = dedup_ratio_;
+        d["hot_rows"] = hot_rows_;
+        d["hot_replica_bytes"] = dev_replica_bytes_;
+        d["hot_replica_active"] = hot_active_;
         return d;
+    }
+
+    // Hot-prefix replica.  replica_view() is this rank's replica region as a
+    // [sum(hot_rows), row_bytes] uint8 tensor (valid until close()); the
+    // buffer fills it after write() through ordinary fetches, with the replica
+    // switched off so those fetches read the owners.
+    torch::Tensor replica_view() {
+        check(connected_ && !closed_, "runtime is not connected");
+        const int64_t rows = int64_t(dev_replica_bytes_ / (row_bytes_ ? row_bytes_ : 1));
+        auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device_);
+        return torch::from_blob(reinterpret_cast<void *>(arena_->ptr() + dev_replica_), {rows, int64_t(row_bytes_)},
+                                opts);
+    }
+
+    void set_hot_active(bool on) {
+        check(connected_ && !closed_, "runtime is not connected");
+        hot_active_ = on && dev_replica_bytes_ > 0;
+        for (uint32_t l = 0; l < layers_; ++l) {
+            const uint32_t v = hot_active_ ? hot_rows_[l] : 0;
+            gather_.layer.hot_rows[l] = v;
+            dispatch_.layer.hot_rows[l] = v;
+            dedup_.layer.hot_rows[l] = v;
+        }
     }
 
     // Synchronous snapshot of the per-(layer, owner) counters (tests only).
@@ -776,6 +819,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             lt.entries[l] = entries_[l];
             lt.table_bases[l] = table_bases_[l];
             lt.sf_bases[l] = sf_bases_[l];
+            lt.hot_rows[l] = hot_active_ ? hot_rows_[l] : 0;
+            lt.hot_bases[l] = hot_bases_[l];
         }
         const uint64_t arena = arena_->ptr();
         GatherParams &g = gather_;
@@ -784,6 +829,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.sf_output = reinterpret_cast<float *>(arena + dev_sf_output_);
         g.error = sink();
         g.layer = lt;
+        g.hot_base = arena + dev_replica_;
         for (uint32_t o = 0; o < world_; ++o) {
             if (o == rank_)
                 g.direct_base[o] = egm_ ? arena + dev_mirror_ : host_->ptr();
@@ -966,6 +1012,11 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     // kDedupProbeEvery fetches while off)
     int dedup_mode_ = 2;
     size_t dev_dedup_ = 0, dev_dedup_bytes_ = 0;
+    // hot-prefix replication: global ids [0, hot_rows_[l]) of layer l are read
+    // from the local replica once it is filled (hot_active_)
+    size_t dev_replica_ = 0, dev_replica_bytes_ = 0;
+    std::vector<uint32_t> hot_rows_, hot_bases_;
+    bool hot_active_ = false;
     uint32_t *dedup_state_ = nullptr, *dedup_stats_ = nullptr, *dedup_stats_dev_ = nullptr;
     uint32_t dedup_slots_ = 0, dedup_seen_epoch_ = 0, dedup_since_probe_ = 0;
     double dedup_ratio_ = -1.0;
@@ -1213,6 +1264,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("debug_stop_service", &Runtime::debug_stop_service)
         .def("debug_peer_copy", &Runtime::debug_peer_copy)
         .def("debug_litmus_reset", &Runtime::debug_litmus_reset)
+        .def("replica_view", &Runtime::replica_view)
+        .def("set_hot_active", &Runtime::set_hot_active)
         .def("debug_litmus", &Runtime::debug_litmus, py::arg("peer"), py::arg("role"), py::arg("epochs"),
              py::arg("words"), py::arg("ctas") = 32, py::arg("weak_loads") = false, py::arg("timeout_ms") = 2000.0)
         .def("close", &Runtime::close)

@@ -42,7 +42,7 @@ import torch.distributed as dist
 
 from . import _native
 from .base import EngramBufferBase, accept_legacy_storage_size
-from .layout import plan_memory, storage_size_hint, validate_config
+from .layout import hot_rows_for, plan_memory, storage_size_hint, validate_config
 from .routing import (
     EgmConfig,
     OwnerRoute,
@@ -79,6 +79,16 @@ def theoretical_config(world, num_layers, num_max_tokens, num_entries_per_token,
     while depth < min(32768, num_max_tokens * num_entries_per_token):
         depth *= 2
     return channels, depth, False
+
+
+def _hot_rows_env() -> str:
+    """``ENGRAM_HOT_ROWS``: replicate global ids ``[0, H)`` of each layer on
+    every rank (one count, or one per layer, comma-separated; default off).
+    Skewed traffic whose hot ids are a low prefix (frequency-ordered
+    vocabularies, Zipf over ids) then reads them from local HBM instead of
+    the hot owner's NVLink.
+    """
+    return os.environ.get("ENGRAM_HOT_ROWS", "")
 
 
 def _gather_kernel() -> str:
@@ -152,6 +162,7 @@ class EngramBuffer(EngramBufferBase):
         self.num_gpu_timeout_secs = float(num_gpu_timeout_secs)
         self.runtime = self.context = None
         self.routes = [OwnerRoute.HOST] * self.num_ranks
+        self.hot_rows = []  # per-layer replicated id prefixes (ENGRAM_HOT_ROWS), set by set_config
         self.owner_fallback_reasons = [""] * self.num_ranks
 
         nodes = [None] * self.num_ranks
@@ -180,13 +191,14 @@ class EngramBuffer(EngramBufferBase):
                               dtype=torch.bfloat16, num_sf_packs=0):
         """``(device_bytes, host_bytes)`` this rank needs for the configuration.
 
-        Depends on ``ENGRAM_EGM_ENABLE`` (an HBM mirror of the shard is added)
-        and ``ENGRAM_WRITE_LOCAL_SF`` (full vs. own-rows scale table).
+        Depends on ``ENGRAM_EGM_ENABLE`` (an HBM mirror of the shard is added),
+        ``ENGRAM_WRITE_LOCAL_SF`` (full vs. own-rows scale table) and
+        ``ENGRAM_HOT_ROWS`` (a replica of each layer's hot id prefix).
         """
         egm = EgmConfig.from_env().enabled
         return storage_size_hint(num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype,
                                  num_sf_packs, group.size(), egm, env_flag("ENGRAM_WRITE_LOCAL_SF", egm),
-                                 _dedup_mode() != 0)
+                                 _dedup_mode() != 0, _hot_rows_env())
 
     @staticmethod
     def get_theoretical_config(group, num_layers, num_max_tokens, num_entries_per_token,
@@ -202,7 +214,8 @@ class EngramBuffer(EngramBufferBase):
             raise RuntimeError("Buffer is destroyed")
         cfg = self._check_config_args(num_entries_per_layer, hidden, num_max_tokens, num_entries_per_token, dtype,
                                       num_sf_packs)
-        plan = plan_memory(cfg, self.num_ranks, self.egm.enabled, self.local_sf, _dedup_mode() != 0)
+        self.hot_rows = hot_rows_for(cfg, self.num_ranks, _hot_rows_env())
+        plan = plan_memory(cfg, self.num_ranks, self.egm.enabled, self.local_sf, _dedup_mode() != 0, self.hot_rows)
         if plan.device_bytes > self.num_gpu_bytes or plan.host_bytes > self.num_rdma_storage_bytes:
             raise ValueError("Insufficient capacity: use EngramBuffer.get_storage_size_hint")
         tokens = [None] * self.num_ranks
@@ -220,6 +233,7 @@ class EngramBuffer(EngramBufferBase):
             gather_strided=env_int("ENGRAM_GATHER_STRIDED", 0, minimum=0),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
+            hot_rows=list(self.hot_rows),
         )
         native = None
         with torch.cuda.device(self.device):
@@ -292,6 +306,41 @@ class EngramBuffer(EngramBufferBase):
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         self._written = True
+        if any(self.hot_rows):
+            self._refresh_replica()
+            dist.barrier(group=self.group)
+
+    def _refresh_replica(self):
+        """Fill this rank's replica of the hot id prefixes from the owners.
+
+        The replica is switched off, then ids ``[0, hot_rows[l])`` are fetched
+        through the ordinary routes in capacity-sized chunks and copied into
+        the replica; then reads of those ids go local.  Runs inside write()
+        (every rank at once), so the owners' data is final.
+        """
+        c = self._config
+        rt = self.runtime
+        rt.set_hot_active(False)
+        replica = rt.replica_view()
+        bases = [sum(self.hot_rows[:l]) for l in range(c.layers)]
+        chunk = c.capacity
+        with torch.cuda.device(self.device):
+            for start in range(0, max(self.hot_rows), chunk):
+                idx = torch.full((c.layers, c.max_tokens, c.ept), -1, dtype=torch.int32, device="cuda")
+                flat = idx.view(c.layers, -1)
+                counts = [max(0, min(chunk, hot - start)) for hot in self.hot_rows]
+                for layer, n in enumerate(counts):
+                    if n:
+                        flat[layer, :n] = torch.arange(start, start + n, dtype=torch.int32, device="cuda")
+                outs = [h() for h in self.fetch(idx)]
+                for layer, n in enumerate(counts):
+                    if n:
+                        data = outs[layer][0] if c.num_sf_packs else outs[layer]
+                        rows = data.view(torch.uint8).reshape(-1, c.row_bytes)[:n]
+                        replica[bases[layer] + start: bases[layer] + start + n].copy_(rows)
+            torch.cuda.synchronize()
+        rt.check_health()  # a failed fill raises here instead of serving a broken replica
+        rt.set_hot_active(True)
 
     # ------------------------------------------------------------------- fetch
     def fetch(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):

@@ -145,10 +145,13 @@ def dedup_table_slots(config: EngramConfig) -> int:
     return 1 << (need - 1).bit_length()
 
 
-def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, dedup: bool = True) -> MemoryPlan:
+def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, dedup: bool = True,
+                hot_rows=None) -> MemoryPlan:
     """Lay out one rank's host shard and device arena.
 
     ``mirror``: keep an HBM copy of the vocabulary for the peer-HBM route.
+    ``hot_rows``: per-layer counts of the global-id prefix replicated on
+    every rank (a ``replica`` region of ``sum(hot_rows)`` rows).
     ``local_sf``: every rank holds the full global FP8 scale table
     (``ENGRAM_WRITE_LOCAL_SF=1``); otherwise each rank holds the scales of its own
     rows only (on one NVLink node that is the node-local shard of the reference,
@@ -178,6 +181,7 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, 
         # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32, layer_arrivals[L] u32,
         # serve claim/finish/board [W*L] u64 each, device error record, alignment slack
         ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 16 + 256),
+        ("replica", sum(hot_rows or ()) * c.row_bytes),
     ]
     off = 0
     for name, size in regions:
@@ -195,9 +199,31 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, 
     return plan
 
 
-def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf, dedup=True):
+def hot_rows_for(config: EngramConfig, world: int, spec) -> list:
+    """Per-layer replicated prefix lengths from ``ENGRAM_HOT_ROWS``-style input.
+
+    ``spec``: ``None``/``""``/``0`` (off), one count for every layer, or one
+    count per layer (comma-separated string or sequence).  Each count is
+    clamped to the layer's ``world * n_l`` global rows.
+    """
+    if spec is None or spec == "":
+        values = [0] * config.layers
+    elif isinstance(spec, str):
+        parts = [int(v) for v in spec.split(",") if v.strip()]
+        values = parts * config.layers if len(parts) == 1 else parts
+    elif isinstance(spec, int):
+        values = [spec] * config.layers
+    else:
+        values = [int(v) for v in spec]
+    if len(values) != config.layers or min(values) < 0:
+        raise ValueError("hot rows: give one non-negative count, or one per layer")
+    return [min(v, n * world) for v, n in zip(values, config.entries)]
+
+
+def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf, dedup=True,
+                      hot_rows=None):
     cfg = validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world)
-    plan = plan_memory(cfg, world, mirror, local_sf, dedup)
+    plan = plan_memory(cfg, world, mirror, local_sf, dedup, hot_rows_for(cfg, world, hot_rows))
     return plan.device_bytes, plan.host_bytes
 
 

@@ -252,6 +252,35 @@ def _dead_owner_times_out(rank, world):
     buf.destroy()
 
 
+def _hot_replica(rank, world):
+    from engram_rdma_lab_b200.models import make_indices, pattern_shard
+
+    _setup(rank)
+    entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
+    os.environ["ENGRAM_HOT_ROWS"] = "30000"  # spans owners 0 and 1
+    try:
+        for egm in (True, False):  # the replica fills through either route
+            buf = _buffer(entries, hidden, 512, ept, dtype, packs, egm=egm, local_sf=True)
+            assert buf.hot_rows == [30000, 30000]
+            for salt in (0, 3):
+                storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda", salt=salt)
+                buf.write(storages, scales)
+                for epoch in range(3):
+                    idx = make_indices(rank, world, entries, 512, ept, epoch=epoch, padding=0.02,
+                                       distribution="zipf" if epoch else "uniform", device="cuda")
+                    outs = [h() for h in buf.fetch(idx)]
+                    torch.cuda.synchronize()
+                    _check(outs, idx, entries, hidden, dtype, packs, salt=salt)
+            dist.barrier()
+            buf.destroy()
+    finally:
+        os.environ.pop("ENGRAM_HOT_ROWS", None)
+
+
+def test_hot_prefix_replica(port):
+    run_ranks(_hot_replica, _world(), port)
+
+
 def _litmus(rank, world):
     _setup(rank)
     buf = _buffer((4099, 4111), 256, 512, 24, torch.bfloat16, 0, egm=True)

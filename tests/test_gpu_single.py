@@ -322,3 +322,28 @@ def test_flag_protocol_litmus_one_gpu(weak_loads):
             rt.debug_litmus(0, "producer", 1, 64)
     finally:
         buf.destroy()
+
+
+@pytest.mark.parametrize("kernel", ["simt", "bulk"])
+def test_hot_prefix_replica_follows_rewrites(kernel, monkeypatch):
+    monkeypatch.setenv("ENGRAM_GATHER_KERNEL", kernel)
+    monkeypatch.setenv("ENGRAM_HOT_ROWS", "3000,700")
+    entries, hidden, ept, dtype, packs = (5003, 5009), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 256, ept, dtype, packs, True)
+    try:
+        assert buf.hot_rows == [3000, 700]
+        mem = buf.memory_usage()
+        assert mem["hot_replica_bytes"] == 3700 * 256 and not mem["hot_replica_active"]
+        for salt in (0, 5):  # a rewrite must refresh the replica
+            storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda", salt=salt)
+            buf.write(storages, scales)
+            assert buf.memory_usage()["hot_replica_active"]
+            for epoch in range(3):
+                idx = make_indices(0, 1, entries, 256, ept, epoch=epoch, distribution="zipf", padding=0.02,
+                                   device="cuda")
+                assert int((idx[0] < 3000).sum()) > 0
+                outs = [h() for h in buf.fetch(idx)]
+                torch.cuda.synchronize()
+                check(outs, idx, entries, hidden, dtype, packs, salt=salt)
+    finally:
+        buf.destroy()

@@ -185,3 +185,21 @@ def test_numa_locality_from_fake_sysfs(tmp_path):
         assert not info["bound"] and os.sched_getaffinity(0) == {allowed[0]}
     finally:
         os.sched_setaffinity(0, before)
+
+
+def test_hot_rows_spec_and_replica_region():
+    from engram_rdma_lab_b200.layout import hot_rows_for
+
+    cfg = validate_config([100, 200], 64, 8, 2, torch.bfloat16, 0, world=4)
+    assert hot_rows_for(cfg, 4, "") == [0, 0]
+    assert hot_rows_for(cfg, 4, "50") == [50, 50]
+    assert hot_rows_for(cfg, 4, "1000,30") == [400, 30]  # clamped to world * n
+    assert hot_rows_for(cfg, 4, [5, 6]) == [5, 6]
+    with pytest.raises(ValueError):
+        hot_rows_for(cfg, 4, "1,2,3")
+    plan = plan_memory(cfg, 4, True, False, hot_rows=[400, 30])
+    assert plan.device["replica"][1] == 430 * 128
+    spans = sorted((off, off + size) for off, size in plan.device.values())
+    assert all(a1 <= b0 for (a0, a1), (b0, b1) in zip(spans, spans[1:]))
+    assert storage_size_hint([100, 200], 64, 8, 2, torch.bfloat16, 0, 4, True, False, hot_rows="400,30")[0] == (
+        plan.device_bytes)

@@ -45,12 +45,18 @@ def test_owner_service_serves_in_sequence():
     assert h.error() == ""
 
 
-def test_owner_service_latches_sequence_error():
+def test_owner_service_accepts_forward_jumps_and_latches_backward_sequence():
     h = C.OwnerServiceHarness(2, 1, 64, [0, 1])
     h.start()
-    h.publish(1, 0, 2, 5, 1)  # skipped epoch 1
+    h.publish(1, 0, 1, 5, 1)
+    assert _wait(lambda: len(h.launched()) == 1)
+    # Epochs 2-3 were finished by the owner's hooks before the thread looked.
+    h.publish(1, 0, 4, 6, 1)
+    assert _wait(lambda: len(h.launched()) == 2)
+    assert (1, 0, 6, 4, 1) in h.launched() and h.error() == ""
+    h.publish(1, 0, 2, 5, 1)  # backwards
     assert _wait(lambda: h.error() != "")
-    assert "sequence" in h.error()
+    assert "backwards" in h.error()
     assert not h.running
     with pytest.raises(RuntimeError):
         h.check()
