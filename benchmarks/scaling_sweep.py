@@ -59,6 +59,7 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--with-baseline", action="store_true")
+    p.add_argument("--hot-rows", default="", help="ENGRAM_HOT_ROWS for our buffer (hot-prefix replica)")
     args = p.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -67,6 +68,8 @@ def main():
                             timeout=datetime.timedelta(seconds=300))
     os.environ["ENGRAM_EGM_ENABLE"] = "1"
     os.environ.setdefault("ENGRAM_WRITE_LOCAL_SF", "1")
+    if args.hot_rows:
+        os.environ["ENGRAM_HOT_ROWS"] = args.hot_rows
     entries, hidden, ept, packs, dtype = (524288, 524288), 256, 24, 2, torch.float8_e4m3fn
     token_list = [int(t) for t in args.tokens.split(",")]
     cap = max(token_list)
@@ -86,6 +89,7 @@ def main():
                 nbytes = len(entries) * tokens * ept * hidden
                 if rank == 0:
                     print(json.dumps({"impl": name, "gpus": world, "tokens": tokens, "distribution": dist_name,
+                                      "hot_rows": getattr(buf, "hot_rows", None) or None,
                                       "per_requester_gbs": round(nbytes / (mean * 1e-3) / 1e9, 1),
                                       "mean_us": round(mean * 1e3, 1), "p50_us": round(p50 * 1e3, 1),
                                       "p99_us": round(p99 * 1e3, 1)}), flush=True)

@@ -81,6 +81,8 @@ def parse():
     p.add_argument("--async-check", action="store_true")
     p.add_argument("--async-eager", action="store_true")
     p.add_argument("--overlap-gemm", default="", help="M,N,K of a bf16 GEMM overlapped on another stream (empty = off)")
+    p.add_argument("--pinned-indices", action="store_true",
+                   help="hand fetch a pinned host copy of each round's indices (eager rounds only)")
     p.add_argument("--profile", action="store_true")
     p.add_argument("--profile-rank", type=int, default=0)
     p.add_argument("--egm-fail-pair", type=parse_pair, action="append", default=[])
@@ -96,6 +98,8 @@ def parse():
         p.error("--async-eager needs --async-check and excludes --cuda-graph")
     if a.traffic != "all-to-all" and (a.async_check or a.profile or a.check_errors or a.locality_cycle):
         p.error("single-requester traffic runs the ordinary or graph benchmark only")
+    if a.pinned_indices and (a.cuda_graph or a.async_check or a.profile or a.impl != "native"):
+        p.error("--pinned-indices runs eager rounds of the native buffer only")
     return a
 
 
@@ -343,9 +347,12 @@ def main():
                                     e2e_ms=None, gbps=None))
                 dist.barrier(group=control)
                 continue
+            # --pinned-indices: the fetch reads a pinned host copy in place
+            # (its PCIe transfer is inside the timed region).
+            source = indices.cpu().pin_memory() if args.pinned_indices else indices
             start = time.perf_counter_ns()
             if graph is None:
-                outputs = forward(indices)
+                outputs = forward(source)
             else:
                 graph.replay()
             torch.cuda.synchronize()
@@ -369,6 +376,7 @@ def main():
         col_major_sf=not args.row_major_sf, traffic=args.traffic, requester_active=active, owner_rank=owner,
         cuda_graph=graph is not None, injected_probe_failures=args.egm_fail_pair, forward_submissions=submissions,
         locality_cycle=args.locality_cycle, rewrite=args.rewrite, cpu_write=args.cpu_write,
+        pinned_indices=args.pinned_indices, hot_rows=getattr(buffer, "hot_rows", None),
     )
     root = Path(args.output_dir)
     root.mkdir(parents=True, exist_ok=True)

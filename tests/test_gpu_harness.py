@@ -27,6 +27,8 @@ SCENARIOS = {
     "single_owner_traffic": SMALL + ["--dtype", "bf16", "--traffic", "single", "--requester-rank", "0",
                                      "--owner-rank", "1", "--distribution", "matched"],
     "torch_baseline": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--impl", "torch", "--padding", "0.05"],
+    "pinned_indices_zipf": SMALL + ["--dtype", "fp8", "--sf-packs", "1", "--pinned-indices", "--distribution",
+                                    "zipf", "--padding", "0.05"],
 }
 
 
@@ -40,6 +42,8 @@ def test_harness_scenario(name, tmp_path):
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     meta = json.loads((out / "engram-r0.json").read_text())["metadata"]
+    if name == "pinned_indices_zipf":
+        assert meta["pinned_indices"] is True
     if name == "probe_fault_fallback":
         assert meta["routing"]["owner_routes"] == ["peer_hbm", "host"]
         assert "0->1" in meta["routing"]["owner_fallback_reasons"][1]
