@@ -336,6 +336,29 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         check_cuda(cudaDeviceSynchronize(), "write synchronise");
     }
 
+    // Copy of layer `layer` as stored on this rank (checkpoints): the host
+    // shard's rows and the scale rows this rank holds (all `world * n` with a
+    // full local scale table, else its own `n`).  Quiesced like write().
+    py::tuple read_layer(uint32_t layer) {
+        check_health();
+        check(ready_ && !closed_, "runtime not ready");
+        check(layer < layers_, "layer out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaDeviceSynchronize(), "read_layer synchronise");
+        const int64_t n = entries_[layer];
+        auto rows = torch::empty({n, int64_t(row_bytes_)}, torch::TensorOptions().dtype(torch::kUInt8));
+        std::memcpy(rows.data_ptr(), static_cast<const uint8_t *>(host_->host_ptr()) + size_t(table_bases_[layer]) * row_bytes_,
+                    size_t(n) * row_bytes_);
+        if (!packs_)
+            return py::make_tuple(rows, py::none());
+        const int64_t sf_rows = n * (local_sf_ ? world_ : 1);
+        auto scales = torch::empty({sf_rows, int64_t(packs_)}, torch::TensorOptions().dtype(torch::kFloat32));
+        const void *src = reinterpret_cast<const uint8_t *>(arena_->ptr()) + dev_sf_table_ + size_t(sf_bases_[layer]) * 4;
+        check_cuda(cudaMemcpy(scales.data_ptr(), src, size_t(sf_rows) * packs_ * 4, cudaMemcpyDeviceToHost),
+                   "read scale table");
+        return py::make_tuple(rows, scales);
+    }
+
     // ------------------------------------------------------------------ fetch
     // The kernels read `indices` on the current stream.  A device tensor is
     // recorded on that stream for the caching allocator.  A pinned host
@@ -1265,6 +1288,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("debug_peer_copy", &Runtime::debug_peer_copy)
         .def("debug_litmus_reset", &Runtime::debug_litmus_reset)
         .def("replica_view", &Runtime::replica_view)
+        .def("read_layer", &Runtime::read_layer)
         .def("set_hot_active", &Runtime::set_hot_active)
         .def("debug_litmus", &Runtime::debug_litmus, py::arg("peer"), py::arg("role"), py::arg("epochs"),
              py::arg("words"), py::arg("ctas") = 32, py::arg("weak_loads") = false, py::arg("timeout_ms") = 2000.0)

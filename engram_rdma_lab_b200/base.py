@@ -58,6 +58,58 @@ class EngramBufferBase(ABC):
         self._input = None
         self._destroyed = False
 
+    # -------------------------------------------------------------- checkpoint
+    STATE_FORMAT = 1
+
+    @abstractmethod
+    def _read_layer(self, layer: int):
+        """``(rows uint8 [n_l, row_bytes], stored scales fp32 [rows, packs] | None)`` on the CPU."""
+
+    def state_dict(self) -> dict:
+        """This rank's vocabulary shard and scales, on the CPU, for a checkpoint.
+
+        Not collective.  ``storages[l]`` is ``[n_l, hidden]`` in the table
+        dtype and ``sfs[l]`` the global-shaped ``[world * n_l, packs]`` scale
+        table ``write()`` takes (rows this rank does not store are zero when
+        ``ENGRAM_WRITE_LOCAL_SF=0``).  The reference has no checkpoint path;
+        ``write()`` is its only loader, and ``load_state_dict`` calls it.
+        """
+        self._ready()
+        if not self._written:
+            raise RuntimeError("write() must initialize the vocabulary before state_dict()")
+        if self._pending:
+            raise RuntimeError("Call all outstanding hooks before state_dict()")
+        c = self._config
+        storages, sfs = [], []
+        for layer, n in enumerate(c.entries):
+            rows, stored = self._read_layer(layer)
+            storages.append(rows.reshape(n, c.row_bytes).view(c.dtype).reshape(n, c.hidden))
+            if c.num_sf_packs:
+                if stored.shape[0] == self.num_ranks * n:
+                    sfs.append(stored.reshape(self.num_ranks * n, c.num_sf_packs))
+                else:
+                    full = torch.zeros(self.num_ranks * n, c.num_sf_packs, dtype=torch.float32)
+                    full[self.rank_idx * n:(self.rank_idx + 1) * n] = stored.reshape(n, c.num_sf_packs)
+                    sfs.append(full)
+        return dict(
+            format=self.STATE_FORMAT, rank=self.rank_idx, world=self.num_ranks,
+            config=dict(entries=list(c.entries), hidden=c.hidden, dtype=str(c.dtype), num_sf_packs=c.num_sf_packs),
+            storages=storages, sfs=sfs if c.num_sf_packs else None,
+        )
+
+    def load_state_dict(self, state: dict):
+        """Collective: restore a ``state_dict()`` of the same rank and table shape via ``write()``."""
+        self._ready()
+        c = self._config
+        want = dict(entries=list(c.entries), hidden=c.hidden, dtype=str(c.dtype), num_sf_packs=c.num_sf_packs)
+        if state.get("format") != self.STATE_FORMAT:
+            raise ValueError("Unknown Engram state format")
+        if state.get("rank") != self.rank_idx or state.get("world") != self.num_ranks:
+            raise ValueError("State belongs to another rank or world size")
+        if state.get("config") != want:
+            raise ValueError(f"State table shape {state.get('config')} does not match {want}")
+        self.write(state["storages"], state["sfs"])
+
     # ------------------------------------------------------------------ checks
     def _ready(self):
         if self._destroyed or not self._configured:

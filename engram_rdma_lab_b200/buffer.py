@@ -310,6 +310,10 @@ class EngramBuffer(EngramBufferBase):
             self._refresh_replica()
             dist.barrier(group=self.group)
 
+    def _read_layer(self, layer):
+        rows, scales = self.runtime.read_layer(layer)
+        return rows, scales
+
     def _refresh_replica(self):
         """Fill this rank's replica of the hot id prefixes from the owners.
 

@@ -148,6 +148,15 @@ class TorchEngramBuffer(EngramBufferBase):
         dist.barrier(group=self.group)
         self._written = True
 
+    def _read_layer(self, layer):
+        c = self._config
+        base, n = c.table_bases()[layer], c.entries[layer]
+        rows = self._table[base:base + n].cpu()
+        if not c.num_sf_packs:
+            return rows, None
+        sf_base = self._plan.sf_bases[layer] // c.num_sf_packs
+        return rows, self._sf_table[sf_base:sf_base + self._plan.sf_rows_per_layer[layer]].cpu()
+
     # ------------------------------------------------------------------- fetch
     def fetch(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
         """Exchange requests and rows with all_to_all; returns one hook per layer."""

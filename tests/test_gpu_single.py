@@ -347,3 +347,29 @@ def test_hot_prefix_replica_follows_rewrites(kernel, monkeypatch):
                 check(outs, idx, entries, hidden, dtype, packs, salt=salt)
     finally:
         buf.destroy()
+
+
+@pytest.mark.parametrize("local_sf", [False, True])
+def test_state_dict_roundtrip_native(local_sf):
+    import io
+
+    entries, hidden, ept, dtype, packs = (3001, 3011), 256, 8, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 128, ept, dtype, packs, True, local_sf=local_sf)
+    storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda", salt=11)
+    buf.write(storages, scales)
+    blob = io.BytesIO()
+    torch.save(buf.state_dict(), blob)
+    buf.destroy()
+    fresh = make_buffer(entries, hidden, 128, ept, dtype, packs, True, local_sf=local_sf)
+    try:
+        state = torch.load(io.BytesIO(blob.getvalue()))
+        for layer in range(2):
+            assert torch.equal(state["storages"][layer].view(torch.uint8), storages[layer].cpu().view(torch.uint8))
+            assert torch.equal(state["sfs"][layer], scales[layer].cpu())
+        fresh.load_state_dict(state)
+        idx = make_indices(0, 1, entries, 128, ept, epoch=3, padding=0.05, device="cuda")
+        outs = [h() for h in fresh.fetch(idx)]
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs, salt=11)
+    finally:
+        fresh.destroy()

@@ -136,3 +136,37 @@ def _config_errors(rank, world):
 
 def test_oracle_config_errors(port):
     run_ranks(_config_errors, 2, port)
+
+
+def _state_roundtrip(rank, world, local_sf):
+    import io
+
+    spec = CONFIGS["oracle"]
+    dtype, packs = torch.float8_e4m3fn, 2
+    buf = _make(world, spec, dtype, packs, local_sf)
+    storages, scales = pattern_shard(rank, world, spec.entries, spec.hidden, dtype, packs, "cpu", salt=7)
+    buf.write(storages, scales)
+    blob = io.BytesIO()
+    torch.save(buf.state_dict(), blob)
+    buf.destroy()
+    fresh = _make(world, spec, dtype, packs, local_sf)
+    state = torch.load(io.BytesIO(blob.getvalue()))
+    for layer in range(len(spec.entries)):
+        assert torch.equal(state["storages"][layer].view(torch.uint8), storages[layer].view(torch.uint8))
+        n = spec.entries[layer]
+        mine = slice(rank * n, (rank + 1) * n)
+        assert torch.equal(state["sfs"][layer][mine], scales[layer][mine])
+        if local_sf == "1":
+            assert torch.equal(state["sfs"][layer], scales[layer])
+    bad = dict(state, rank=1 - rank)
+    with pytest.raises(ValueError):
+        fresh.load_state_dict(bad)
+    fresh.load_state_dict(state)
+    idx = make_indices(rank, world, spec.entries, spec.tokens, spec.ept, padding=spec.padding)
+    _check([h() for h in fresh.fetch(idx)], idx, spec, dtype, packs, salt=7)
+    fresh.destroy()
+
+
+@pytest.mark.parametrize("local_sf", ["0", "1"])
+def test_state_dict_roundtrip_world2(port, local_sf):
+    run_ranks(_state_roundtrip, 2, port, args=(local_sf,))
