@@ -1,0 +1,93 @@
+// Standalone operators of the extension: the per-owner request pack (the
+// dispatch kernel aimed at caller-owned buffers) and the NVTX switch.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "bindings.h"
+#include "driver.h"
+#include "kernels/params.h"
+#include "trace.h"
+
+namespace py = pybind11;
+
+namespace engram {
+
+namespace {
+
+// Standalone per-owner pack (the dispatch kernel aimed at local buffers).
+// packed: int64 [world, layers, capacity]; counts: int32 [layers, world];
+// scratch: int32 with at least layers * world * 4 + layers elements, owned by
+// the caller (cursors, arrival counters, epochs).  Owners with owners[o] == 0
+// are skipped.  Within one owner the order of entries is not specified.
+void route_pack(const torch::Tensor &indices, const std::vector<uint32_t> &entries, uint32_t world,
+                const std::vector<uint8_t> &owners, torch::Tensor &packed, torch::Tensor &counts,
+                torch::Tensor &scratch) {
+    check(indices.is_cuda() && indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_contiguous(),
+          "indices must be contiguous CUDA int32 [layers, tokens, ept]");
+    const uint32_t layers = uint32_t(indices.size(0)), rows = uint32_t(indices.size(1) * indices.size(2));
+    check(layers >= 1 && layers <= kMaxLayers && entries.size() == layers, "layers");
+    check(world >= 1 && world <= kMaxRanks && owners.size() == world, "world");
+    check(packed.is_cuda() && packed.scalar_type() == torch::kLong && packed.is_contiguous() && packed.dim() == 3 &&
+              packed.size(0) == world && packed.size(1) == layers && packed.size(2) >= rows,
+          "packed must be contiguous CUDA int64 [world, layers, capacity >= tokens*ept]");
+    check(counts.is_cuda() && counts.scalar_type() == torch::kInt && counts.is_contiguous() &&
+              counts.numel() == int64_t(layers) * world,
+          "counts must be contiguous CUDA int32 [layers, world]");
+    const size_t lw = size_t(layers) * world;
+    check(scratch.is_cuda() && scratch.scalar_type() == torch::kInt && scratch.is_contiguous() &&
+              size_t(scratch.numel()) >= lw * 4 + layers,
+          "scratch must be contiguous CUDA int32 with layers*world*4 + layers elements");
+    const int dev = indices.get_device();
+    check(packed.get_device() == dev && counts.get_device() == dev && scratch.get_device() == dev, "devices");
+    c10::cuda::CUDAGuard guard(dev);
+    cudaStream_t s = at::cuda::getCurrentCUDAStream(dev).stream();
+    DispatchParams d{};
+    uint32_t at = 0;
+    for (uint32_t l = 0; l < layers; ++l) {
+        check(entries[l] > 0 && uint64_t(entries[l]) * world <= 0x7FFFFFFFull, "entries");
+        d.layer.entries[l] = entries[l];
+        d.layer.table_bases[l] = at;
+        at += entries[l];
+    }
+    uint32_t *base = reinterpret_cast<uint32_t *>(scratch.data_ptr<int32_t>());
+    d.epochs = reinterpret_cast<uint64_t *>(base);  // 2 * lw words
+    d.cursors = base + 2 * lw;                      // lw words
+    d.layer_arrivals = base + 3 * lw;               // layers words
+    d.totals = reinterpret_cast<uint32_t *>(counts.data_ptr<int32_t>());
+    d.error = ErrorSink{nullptr, nullptr};
+    const uint64_t cap = uint64_t(packed.size(2));
+    for (uint32_t o = 0; o < world; ++o)
+        d.inbox_base[o] =
+            owners[o] ? reinterpret_cast<uint64_t>(packed.data_ptr<int64_t>()) + uint64_t(o) * layers * cap * 8 : 0;
+    d.indices = indices.data_ptr<int32_t>();
+    d.layers = layers;
+    d.rows = rows;
+    d.capacity = uint32_t(cap);
+    d.world = world;
+    d.rank = 0;
+    d.channels = 1;
+    d.tile_rows = 512;
+    check_cuda(cudaMemsetAsync(d.cursors, 0, (lw + layers) * 4, s), "clear pack scratch");
+    if (rows == 0) {
+        check_cuda(cudaMemsetAsync(d.totals, 0, lw * 4, s), "clear counts");
+        return;
+    }
+    check_cuda(launch_dispatch(d, s), "launch route pack");
+}
+
+
+} // namespace
+
+void bind_ops(py::module_ &m) {
+    m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),
+          py::arg("packed"), py::arg("counts"), py::arg("scratch"));
+    m.def("set_nvtx", [](bool on) { nvtx_enabled().store(on); }, py::arg("enabled"),
+          "Enable NVTX ranges around fetch, hook, write and owner-service launches.");
+    m.def("nvtx_enabled", []() { return nvtx_enabled().load(); });
+}
+
+} // namespace engram

@@ -25,7 +25,6 @@
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
-#include <sys/mman.h>
 #include <unistd.h>
 
 #include <cstring>
@@ -37,6 +36,7 @@
 #include "fdpass.h"
 #include "kernels/params.h"
 #include "memory.h"
+#include "bindings.h"
 #include "owner_service.h"
 #include "trace.h"
 
@@ -1121,145 +1121,6 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     }
 };
 
-// -------------------------------------------------------------------------
-// CPU test harnesses: the owner service and descriptor passing without a GPU.
-
-class OwnerServiceHarness {
-  public:
-    OwnerServiceHarness(uint32_t world, uint32_t layers, uint32_t capacity, std::vector<uint8_t> serve)
-        : world_(world), layers_(layers), capacity_(capacity), serve_(std::move(serve)),
-          headers_(size_t(world) * layers) {
-        std::memset(headers_.data(), 0, headers_.size() * sizeof(MailboxHeader));
-    }
-    ~OwnerServiceHarness() { service_.stop_and_join(); }
-
-    void publish(uint32_t requester, uint32_t layer, uint64_t epoch, uint32_t rows, uint32_t channels) {
-        MailboxHeader *h = &headers_.at(size_t(requester) * layers_ + layer);
-        __atomic_store_n(&h->rows, rows, __ATOMIC_RELAXED);
-        __atomic_store_n(&h->layer, layer, __ATOMIC_RELAXED);
-        __atomic_store_n(&h->requester, requester, __ATOMIC_RELAXED);
-        __atomic_store_n(&h->channels, channels, __ATOMIC_RELAXED);
-        __atomic_store_n(&h->ready, epoch, __ATOMIC_RELEASE);
-    }
-    void start(int fail_after) {
-        OwnerServiceConfig c;
-        c.world = world_;
-        c.layers = layers_;
-        c.capacity = capacity_;
-        c.headers = headers_.data();
-        c.serve = serve_;
-        c.idle_spin_us = 1000;
-        c.nap_us = 20;
-        fail_after_ = fail_after;
-        service_.start(std::move(c), [this](const std::vector<PushTask> &batch) {
-            std::lock_guard<std::mutex> lock(mu_);
-            for (const auto &t : batch) {
-                if (fail_after_ >= 0 && int(launched_.size()) >= fail_after_)
-                    throw std::runtime_error("injected launch failure");
-                launched_.push_back(t);
-            }
-        });
-    }
-    void stop() {
-        py::gil_scoped_release release;
-        service_.stop_and_join();
-    }
-    py::list launched() {
-        std::lock_guard<std::mutex> lock(mu_);
-        py::list out;
-        for (const auto &t : launched_)
-            out.append(py::make_tuple(t.requester, t.layer, t.rows, t.epoch, t.channels));
-        return out;
-    }
-    std::string error() { return service_.error(); }
-    void check() { service_.check(); }
-    bool running() const { return service_.running(); }
-
-  private:
-    uint32_t world_, layers_, capacity_;
-    std::vector<uint8_t> serve_;
-    std::vector<MailboxHeader> headers_;
-    OwnerService service_;
-    std::mutex mu_;
-    std::vector<PushTask> launched_;
-    int fail_after_ = -1;
-};
-
-// Standalone per-owner pack (the dispatch kernel aimed at local buffers).
-// packed: int64 [world, layers, capacity]; counts: int32 [layers, world];
-// scratch: int32 with at least layers * world * 4 + layers elements, owned by
-// the caller (cursors, arrival counters, epochs).  Owners with owners[o] == 0
-// are skipped.  Within one owner the order of entries is not specified.
-void route_pack(const torch::Tensor &indices, const std::vector<uint32_t> &entries, uint32_t world,
-                const std::vector<uint8_t> &owners, torch::Tensor &packed, torch::Tensor &counts,
-                torch::Tensor &scratch) {
-    check(indices.is_cuda() && indices.dim() == 3 && indices.scalar_type() == torch::kInt && indices.is_contiguous(),
-          "indices must be contiguous CUDA int32 [layers, tokens, ept]");
-    const uint32_t layers = uint32_t(indices.size(0)), rows = uint32_t(indices.size(1) * indices.size(2));
-    check(layers >= 1 && layers <= kMaxLayers && entries.size() == layers, "layers");
-    check(world >= 1 && world <= kMaxRanks && owners.size() == world, "world");
-    check(packed.is_cuda() && packed.scalar_type() == torch::kLong && packed.is_contiguous() && packed.dim() == 3 &&
-              packed.size(0) == world && packed.size(1) == layers && packed.size(2) >= rows,
-          "packed must be contiguous CUDA int64 [world, layers, capacity >= tokens*ept]");
-    check(counts.is_cuda() && counts.scalar_type() == torch::kInt && counts.is_contiguous() &&
-              counts.numel() == int64_t(layers) * world,
-          "counts must be contiguous CUDA int32 [layers, world]");
-    const size_t lw = size_t(layers) * world;
-    check(scratch.is_cuda() && scratch.scalar_type() == torch::kInt && scratch.is_contiguous() &&
-              size_t(scratch.numel()) >= lw * 4 + layers,
-          "scratch must be contiguous CUDA int32 with layers*world*4 + layers elements");
-    const int dev = indices.get_device();
-    check(packed.get_device() == dev && counts.get_device() == dev && scratch.get_device() == dev, "devices");
-    c10::cuda::CUDAGuard guard(dev);
-    cudaStream_t s = at::cuda::getCurrentCUDAStream(dev).stream();
-    DispatchParams d{};
-    uint32_t at = 0;
-    for (uint32_t l = 0; l < layers; ++l) {
-        check(entries[l] > 0 && uint64_t(entries[l]) * world <= 0x7FFFFFFFull, "entries");
-        d.layer.entries[l] = entries[l];
-        d.layer.table_bases[l] = at;
-        at += entries[l];
-    }
-    uint32_t *base = reinterpret_cast<uint32_t *>(scratch.data_ptr<int32_t>());
-    d.epochs = reinterpret_cast<uint64_t *>(base);  // 2 * lw words
-    d.cursors = base + 2 * lw;                      // lw words
-    d.layer_arrivals = base + 3 * lw;               // layers words
-    d.totals = reinterpret_cast<uint32_t *>(counts.data_ptr<int32_t>());
-    d.error = ErrorSink{nullptr, nullptr};
-    const uint64_t cap = uint64_t(packed.size(2));
-    for (uint32_t o = 0; o < world; ++o)
-        d.inbox_base[o] =
-            owners[o] ? reinterpret_cast<uint64_t>(packed.data_ptr<int64_t>()) + uint64_t(o) * layers * cap * 8 : 0;
-    d.indices = indices.data_ptr<int32_t>();
-    d.layers = layers;
-    d.rows = rows;
-    d.capacity = uint32_t(cap);
-    d.world = world;
-    d.rank = 0;
-    d.channels = 1;
-    d.tile_rows = 512;
-    check_cuda(cudaMemsetAsync(d.cursors, 0, (lw + layers) * 4, s), "clear pack scratch");
-    if (rows == 0) {
-        check_cuda(cudaMemsetAsync(d.totals, 0, lw * 4, s), "clear counts");
-        return;
-    }
-    check_cuda(launch_dispatch(d, s), "launch route pack");
-}
-
-int memfd_with_bytes(const std::string &data) {
-    int fd = memfd_create("engram-test", MFD_CLOEXEC);
-    check(fd >= 0, "memfd_create");
-    check(ftruncate(fd, off_t(data.size())) == 0, "ftruncate");
-    check(pwrite(fd, data.data(), data.size(), 0) == ssize_t(data.size()), "pwrite");
-    return fd;
-}
-
-py::bytes read_fd_bytes(int fd, size_t n) {
-    std::string out(n, '\0');
-    check(pread(fd, out.data(), n, 0) == ssize_t(n), "pread");
-    return py::bytes(out);
-}
-
 } // namespace engram
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -1269,7 +1130,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.attr("MAX_LAYERS") = kMaxLayers;
     m.attr("HEADER_BYTES") = kHeaderBytes;
     m.attr("MAX_PUSH_TASKS") = kMaxPushTasks;
-    m.attr("KERNELS") = py::make_tuple("gather_kernel", "dispatch_kernel", "push_kernel", "hook_wait_kernel");
+    m.attr("KERNELS") = py::make_tuple("gather_simt_kernel", "gather_bulk_kernel", "dispatch_kernel", "push_kernel",
+                                       "hook_kernel", "dedup_kernel", "expand_kernel", "litmus_kernel",
+                                       "wait_probe_kernel", "stream_copy_kernel");
     py::class_<Runtime, std::shared_ptr<Runtime>>(m, "Runtime")
         .def(py::init<const py::dict &>())
         .def("bootstrap", &Runtime::bootstrap)
@@ -1294,25 +1157,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              py::arg("words"), py::arg("ctas") = 32, py::arg("weak_loads") = false, py::arg("timeout_ms") = 2000.0)
         .def("close", &Runtime::close)
         .def_property_readonly("closed", &Runtime::closed);
-    py::class_<OwnerServiceHarness>(m, "OwnerServiceHarness")
-        .def(py::init<uint32_t, uint32_t, uint32_t, std::vector<uint8_t>>())
-        .def("publish", &OwnerServiceHarness::publish)
-        .def("start", &OwnerServiceHarness::start, py::arg("fail_after") = -1)
-        .def("stop", &OwnerServiceHarness::stop)
-        .def("launched", &OwnerServiceHarness::launched)
-        .def("error", &OwnerServiceHarness::error)
-        .def("check", &OwnerServiceHarness::check)
-        .def_property_readonly("running", &OwnerServiceHarness::running);
-    py::class_<FdServer>(m, "FdServer")
-        .def(py::init<const std::string &, std::vector<int>>())
-        .def("stop", &FdServer::stop)
-        .def_property_readonly("served", &FdServer::served);
-    m.def("fetch_fd", &fetch_fd, py::arg("name"), py::arg("index"), py::arg("timeout_s") = 30.0);
-    m.def("set_nvtx", [](bool on) { nvtx_enabled().store(on); }, py::arg("enabled"),
-          "Enable NVTX ranges around fetch, hook, write and owner-service launches.");
-    m.def("nvtx_enabled", []() { return nvtx_enabled().load(); });
-    m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),
-          py::arg("packed"), py::arg("counts"), py::arg("scratch"));
-    m.def("memfd_with_bytes", &memfd_with_bytes);
-    m.def("read_fd_bytes", &read_fd_bytes);
+    bind_ops(m);
+    bind_harness(m);
 }
