@@ -271,7 +271,12 @@ class EngramBuffer(EngramBufferBase):
                 except Exception as error:
                     report = {"error": str(error)}
                 self._exchange(report, "commit")
-                native.connect()
+                try:
+                    native.connect()
+                    report = {}
+                except Exception as error:
+                    report = {"error": str(error)}
+                self._exchange(report, "connect")  # every rank raises if one could not start serving
             except Exception:
                 native.close()
                 raise

@@ -2,6 +2,7 @@
 
 import datetime
 import os
+import sys
 import traceback
 
 import torch.distributed as dist
@@ -19,11 +20,18 @@ def _entry(rank, world, port, backend, fn, args, errors):
         dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
         try:
             fn(rank, world, *args)
+            dist.barrier()  # no rank tears its connections down while a peer still uses them
         finally:
             dist.destroy_process_group()
     except BaseException:  # noqa: BLE001 - report everything to the parent
         errors.put((rank, traceback.format_exc()))
         raise
+    # Success: leave without interpreter finalisation.  Process-group
+    # destructors that run at exit while the peer process is exiting too
+    # have aborted a finished rank (SIGABRT) now and then.
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def run_ranks(fn, world, port, backend="gloo", args=(), timeout=300):
