@@ -142,8 +142,6 @@ class EngramBuffer(EngramBufferBase):
         if legacy:
             raise TypeError(f"Unknown arguments: {', '.join(legacy)}")
         super().__init__(group, explicitly_destroy)
-        if not allow_hybrid_mode:
-            raise NotImplementedError("This backend requires node-local shared mappings (allow_hybrid_mode=True)")
         if not 1 <= num_allocated_qps <= 16 or qp_depth < 32:
             raise ValueError("num_allocated_qps must be in [1, 16] and qp_depth >= 32")
         if num_gpu_timeout_secs <= 0:
@@ -152,8 +150,14 @@ class EngramBuffer(EngramBufferBase):
             raise RuntimeError("EngramBuffer needs a CUDA device; use TorchEngramBuffer on CPU")
         self._C = _native.load()
         self.use_cpu_rdma_storage = bool(use_cpu_rdma_storage)
-        self.allow_hybrid_mode = True
+        # Every rank of a buffer shares one NVLink node here, so "hybrid"
+        # (NVLink + RDMA) and pure modes move data the same way; only the
+        # reference's rule for the direct route is kept
+        # (deepep/deep_ep/buffers/engram.py:87-88).
+        self.allow_hybrid_mode = bool(allow_hybrid_mode)
         self.egm = EgmConfig(True) if not self.use_cpu_rdma_storage else EgmConfig.from_env()
+        if self.egm.enabled and not self.allow_hybrid_mode:
+            raise ValueError("The peer-HBM (EGM) route requires allow_hybrid_mode=True")
         self.local_sf = env_flag("ENGRAM_WRITE_LOCAL_SF", self.egm.enabled)
         self.device = torch.cuda.current_device()
         self.num_gpu_bytes, self.num_rdma_storage_bytes = int(num_gpu_bytes), int(num_rdma_storage_bytes)

@@ -68,6 +68,8 @@ class TorchEngramBuffer(EngramBufferBase):
         self.num_gpu_bytes, self.num_rdma_storage_bytes = int(num_gpu_bytes), int(num_rdma_storage_bytes)
         self.use_cpu_rdma_storage = bool(use_cpu_rdma_storage)
         self.allow_hybrid_mode = bool(allow_hybrid_mode)
+        if self.egm.enabled and not self.allow_hybrid_mode:
+            raise ValueError("The peer-HBM (EGM) route requires allow_hybrid_mode=True")
         self.num_allocated_qps, self.qp_depth = int(num_allocated_qps), int(qp_depth)
         self.restrict_rd_atomic, self.sl_idx = restrict_rd_atomic, sl_idx
         self.num_gpu_timeout_secs = num_gpu_timeout_secs

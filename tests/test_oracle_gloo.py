@@ -132,6 +132,13 @@ def _config_errors(rank, world):
     implicit = TorchEngramBuffer(group, *sizes, True, 1, 1024)
     with pytest.raises(RuntimeError):
         implicit.destroy()  # explicitly_destroy=False
+    import os
+
+    os.environ["ENGRAM_EGM_ENABLE"] = "1"
+    with pytest.raises(ValueError, match="allow_hybrid_mode"):
+        TorchEngramBuffer(group, *sizes, True, 1, 1024, allow_hybrid_mode=False)
+    os.environ["ENGRAM_EGM_ENABLE"] = "0"
+    TorchEngramBuffer(group, *sizes, True, 1, 1024, allow_hybrid_mode=False, explicitly_destroy=True).destroy()
 
 
 def test_oracle_config_errors(port):
