@@ -42,7 +42,7 @@ import torch.distributed as dist
 
 from . import _native
 from .base import EngramBufferBase, accept_legacy_storage_size
-from .layout import hot_rows_for, plan_memory, storage_size_hint, validate_config
+from .layout import hot_rows_for, plan_memory, replica_chunks, storage_size_hint, validate_config
 from .routing import (
     EgmConfig,
     OwnerRoute,
@@ -336,12 +336,10 @@ class EngramBuffer(EngramBufferBase):
         rt.set_hot_active(False)
         replica = rt.replica_view()
         bases = [sum(self.hot_rows[:l]) for l in range(c.layers)]
-        chunk = c.capacity
         with torch.cuda.device(self.device):
-            for start in range(0, max(self.hot_rows), chunk):
+            for start, counts in replica_chunks(self.hot_rows, c.capacity):
                 idx = torch.full((c.layers, c.max_tokens, c.ept), -1, dtype=torch.int32, device="cuda")
                 flat = idx.view(c.layers, -1)
-                counts = [max(0, min(chunk, hot - start)) for hot in self.hot_rows]
                 for layer, n in enumerate(counts):
                     if n:
                         flat[layer, :n] = torch.arange(start, start + n, dtype=torch.int32, device="cuda")

@@ -220,6 +220,20 @@ def hot_rows_for(config: EngramConfig, world: int, spec) -> list:
     return [min(v, n * world) for v, n in zip(values, config.entries)]
 
 
+def replica_chunks(hot_rows, capacity: int):
+    """Fetch plan that fills a hot-prefix replica: one entry per fetch.
+
+    Each entry is ``(start, counts)``: that fetch requests global ids
+    ``[start, start + counts[l])`` of layer ``l`` in its first output rows
+    (the rest padding), and those rows go to replica rows ``hot_base[l] +
+    start`` onward.
+    """
+    plan = []
+    for start in range(0, max(hot_rows, default=0), capacity):
+        plan.append((start, [max(0, min(capacity, hot - start)) for hot in hot_rows]))
+    return plan
+
+
 def storage_size_hint(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world, mirror, local_sf, dedup=True,
                       hot_rows=None):
     cfg = validate_config(entries, hidden, max_tokens, ept, dtype, num_sf_packs, world)

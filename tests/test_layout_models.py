@@ -203,3 +203,15 @@ def test_hot_rows_spec_and_replica_region():
     assert all(a1 <= b0 for (a0, a1), (b0, b1) in zip(spans, spans[1:]))
     assert storage_size_hint([100, 200], 64, 8, 2, torch.bfloat16, 0, 4, True, False, hot_rows="400,30")[0] == (
         plan.device_bytes)
+
+
+def test_replica_fill_plan_covers_every_hot_id_once():
+    from engram_rdma_lab_b200.layout import replica_chunks
+
+    assert replica_chunks([0, 0], 100) == []
+    plan = replica_chunks([250, 30, 0], 100)
+    assert [start for start, _ in plan] == [0, 100, 200]
+    assert plan[0][1] == [100, 30, 0] and plan[1][1] == [100, 0, 0] and plan[2][1] == [50, 0, 0]
+    for layer, hot in enumerate([250, 30, 0]):
+        covered = [start + i for start, counts in plan for i in range(counts[layer])]
+        assert covered == list(range(hot))
