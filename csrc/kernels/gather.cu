@@ -1,25 +1,29 @@
-// Requester-side gather (sm_100a): the hot kernel of the peer-HBM route.
+// Requester-side gather (sm_100a): the hot kernel of every fetch.
 //
 // Parity: the reference's direct-read paths, `engram_fetch.cuh:70-101` (READ,
 // EGM rows) + `:223-269` (scale warps) and `gpu_request.cu:214-270`
 // (`issue_egm`, WRITE).  Differences by design:
 //   * the source of a direct row is the owner's HBM mirror reached through
-//     NVLink 5 / NVSwitch (or this rank's own shard), not host memory over C2C;
-//   * rows move with TMA bulk copies (`cp.async.bulk` global -> shared, one
-//     per row, completing on an mbarrier) into an 8-stage shared-memory ring,
-//     so a single producer lane keeps hundreds of rows in flight per SM
-//     without holding registers; a consumer warp streams finished stages to
-//     the final [tokens, hidden*ept] positions, zero-filling padding rows;
-//   * dedicated warps gather the FP8 scales with several independent loads in
-//     flight per lane, writing the column-major layout coalesced;
+//     NVLink 5 / NVSwitch, this rank's own shard, or this rank's replica of
+//     the hot id prefix; never host memory of another rank;
+//   * two variants, picked per buffer (ENGRAM_GATHER_KERNEL=auto|simt|bulk):
+//       - SIMT (default when every direct row is local): each warp owns an
+//         equal contiguous range of rows; one lane resolves each row and LPR
+//         lanes move it with 16-byte loads, UNROLL rows in flight per lane;
+//       - TMA (default when rows come over NVLink): one `cp.async.bulk`
+//         (global -> shared, completing on an mbarrier) per row into an
+//         8-stage shared ring, so one producer lane keeps hundreds of rows in
+//         flight per SM without holding registers; a consumer warp streams
+//         finished stages to the final positions; two scale warps copy each
+//         tile's FP8 scales using the indices the producer left in the stage;
+//   * indices may sit in pinned host memory: both variants stage them ahead
+//     with cp.async, so the PCIe latency overlaps the row copies;
 //   * route tables, layer geometry and strides are kernel parameters
 //     (__grid_constant__), so CUDA Graph replays carry them;
 //   * an out-of-range index is recorded in the error record and zero-filled,
 //     and every barrier wait is bounded; nothing traps.
 // The bulk copies are plain (non-multicast) loads; reading a peer's memory
 // this way is allowed, multicast from peer memory never appears here.
-// A SIMT variant (16-byte vector loads, ENGRAM_GATHER_KERNEL=simt) is kept for
-// rows too large for the shared-memory ring and for A/B measurements.
 #include "params.h"
 #include "ptx.cuh"
 

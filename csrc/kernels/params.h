@@ -81,12 +81,10 @@ struct GatherParams {
     uint64_t direct_base[kMaxRanks];  // per owner; 0 = rows arrive by owner push
     uint64_t sf_base[kMaxRanks];      // per scale shard
     uint64_t hot_base;                // local replica of the hot prefixes (LayerTable::hot_rows)
-    uint32_t layers, rows, tokens, ept;
+    uint32_t layers, rows, ept;
     uint32_t capacity, row_bytes, world, packs;
     uint32_t sf_shard_div;        // global row -> shard: x / (n * sf_shard_div)
-    uint32_t sf_token_stride, sf_hidden_stride, sf_layer_stride;
-    uint32_t col_major_sf;
-    uint32_t sf_warps;            // warps per CTA dedicated to scales (0 for BF16)
+    uint32_t sf_token_stride, sf_hidden_stride, sf_layer_stride;  // either scale layout
     uint32_t variant;             // kGatherBulk or kGatherSimt
     uint32_t ctas_per_sm;         // SIMT grid cap per SM (0 = default 2)
     uint32_t unroll;              // SIMT row-steps in flight for 256-byte rows (0 = default)

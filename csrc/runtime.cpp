@@ -440,11 +440,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             g.dedup = dedup ? 1 : 0;
             g.indices = idx;
             g.rows = rows;
-            g.tokens = tokens_;
             g.sf_token_stride = ts;
             g.sf_hidden_stride = hs;
             g.sf_layer_stride = ls;
-            g.col_major_sf = col_major ? 1 : 0;
             check_cuda(launch_gather(g, num_sms_, s), "launch gather");
             ++launches_;
             if (dedup) {
@@ -875,7 +873,6 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.row_bytes = row_bytes_;
         g.world = world_;
         g.packs = packs_;
-        g.sf_warps = packs_ ? 2 : 0;
         g.variant = gather_variant_;
         const uint32_t slots = dev_dedup_bytes_ ? uint32_t((dev_dedup_bytes_ - size_t(layers_) * capacity_ * 4) / 16) : 0;
         g.dedup_slots = reinterpret_cast<const uint32_t *>(arena + dev_dedup_ + size_t(slots) * 16);
