@@ -14,12 +14,17 @@
 //     because every entry carries its final output position.
 //   * the owner's GPU reads the rows from its host-pinned shard zero-copy and
 //     stores them through NVLink directly into the requester's final output
-//     positions, so the hook has nothing to scatter.
+//     positions, so the hook has nothing to scatter.  A request is split into
+//     256-row chunks claimed by CAS, so push kernels launched by the owner's
+//     CPU service and the owner's own hook kernels (which serve while they
+//     wait) share the work and no GPU spins on work only another launch does.
+//   * ids of a replicated hot prefix are never dispatched: the requester's
+//     gather reads them from its replica.
 //   * per-(layer, owner) epochs advance only for non-empty requests, so empty
 //     layers and idle owners keep requester and owner sequences aligned under
 //     CUDA Graph replay (gpu_request.cu:47-50, 128-130).
-//   * every wait is bounded by the global timer and reports through the error
-//     record; nothing traps.
+//   * every wait is bounded by the global timer and a poll count, and reports
+//     through the error record; nothing traps.
 #include "params.h"
 #include "ptx.cuh"
 

@@ -69,9 +69,11 @@ struct LayerTable {
     uint32_t hot_bases[kMaxLayers];
 };
 
-// Requester-side gather: every row whose owner has a direct source (the
-// owner's HBM mirror through NVLink, or this rank's own shard) is copied into
-// the output; padding rows become zero; FP8 scales are gathered for all rows.
+// Requester-side gather: every row with a direct source (the owner's HBM
+// mirror through NVLink, this rank's own shard, or this rank's replica of the
+// hot id prefix) is copied into the output; padding rows become zero; FP8
+// scales are gathered for all rows.  `indices` may be a device pointer or the
+// device mapping of pinned host memory.
 struct GatherParams {
     const int32_t *indices;       // [layers][rows]
     uint8_t *output;              // [layers][capacity][row_bytes]

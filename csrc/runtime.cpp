@@ -13,7 +13,9 @@
 //     padding, scales) on the caller's stream and return per-layer views;
 //   * wait_layer(): make the caller's stream depend on the fetch, enqueue the
 //     bounded done-flag wait for host-route owners, record the layer event;
-//   * run the owner service that launches push kernels for requesters.
+//   * run the owner service that launches push kernels for requesters;
+//   * keep the optional replica of each layer's hot id prefix and export a
+//     layer's stored rows and scales for checkpoints.
 // Capture-aware event wiring follows the reference (runtime.cpp:412-568): an
 // eager fetch waits for the previous round's per-layer completion events;
 // under capture an internal event joins cross-stream hooks into the graph and
