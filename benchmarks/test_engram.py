@@ -1,7 +1,9 @@
 """Integration test and benchmark entry for the B200 EngramBuffer (one process per GPU).
 
 Run with ``python -m torch.distributed.run --nnodes 1 --nproc-per-node N
---master-addr 127.0.0.1 benchmarks/test_engram.py [options] --output-dir DIR``.
+--master-addr 127.0.0.1 benchmarks/test_engram.py [options] --output-dir DIR``,
+or plainly (``python benchmarks/test_engram.py --local-ranks N ...``) to have
+it spawn N local workers itself.
 
 Scenarios mirror the reference's two entries (``benchmarks/test_read.py``,
 ``benchmarks/test_write.py``): all-to-all, single-owner and single-requester
@@ -62,6 +64,9 @@ def parse():
     p.add_argument("--dtype", choices=["fp8", "bf16"], default="fp8")
     p.add_argument("--sf-packs", type=int, default=2)
     p.add_argument("--qps", type=int, default=0)
+    p.add_argument("--qp-depth", type=int, default=0, help="0 uses the buffer's recommendation")
+    p.add_argument("--local-ranks", type=int, default=2,
+                   help="workers to spawn on this node when not launched by torchrun")
     p.add_argument("--traffic", choices=["all-to-all", "single", "single-requester"], default="all-to-all")
     p.add_argument("--requester-rank", type=int, default=0)
     p.add_argument("--owner-rank", type=int, default=1)
@@ -122,6 +127,26 @@ def inject_probe_failures(rank, pairs):
 
 def main():
     args = parse()
+    if "RANK" not in os.environ:
+        # Not under torchrun: spawn --local-ranks workers on this node, like
+        # the reference's entries do (test_write.py:599-600).
+        import socket
+
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        torch.multiprocessing.spawn(_local_worker, args=(args, port), nprocs=args.local_ranks)
+        return
+    run(args)
+
+
+def _local_worker(local_rank, args, port):
+    os.environ.update(RANK=str(local_rank), LOCAL_RANK=str(local_rank), WORLD_SIZE=str(args.local_ranks),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    run(args)
+
+
+def run(args):
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -148,6 +173,7 @@ def main():
     group = dist.group.WORLD
     sizes = cls.get_storage_size_hint(group, entries, args.hidden, capacity, args.ept, dtype, packs)
     qps, depth, restrict = cls.get_theoretical_config(group, len(entries), capacity, args.ept)
+    depth = args.qp_depth or depth
     buffer = cls(group, *sizes, True, qps, depth, restrict, num_gpu_timeout_secs=args.timeout,
                  explicitly_destroy=True)
     buffer.set_config(entries, args.hidden, capacity, args.ept, dtype, packs)
