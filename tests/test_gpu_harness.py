@@ -47,3 +47,15 @@ def test_harness_scenario(name, tmp_path):
     if name == "probe_fault_fallback":
         assert meta["routing"]["owner_routes"] == ["peer_hbm", "host"]
         assert "0->1" in meta["routing"]["owner_fallback_reasons"][1]
+
+
+def test_harness_spawns_local_ranks_without_torchrun(tmp_path):
+    out = tmp_path / "spawned"
+    cmd = [sys.executable, os.path.join(ROOT, "benchmarks", "test_engram.py"), *SMALL, "--dtype", "bf16",
+           "--local-ranks", "2", "--qp-depth", "512", "--output-dir", str(out)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    env["NCCL_NVLS_ENABLE"] = "0"
+    proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    for rank in range(2):
+        assert (out / f"engram-r{rank}.json").exists()
