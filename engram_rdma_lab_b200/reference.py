@@ -161,11 +161,19 @@ class TorchEngramBuffer(EngramBufferBase):
 
     # ------------------------------------------------------------------- fetch
     def fetch(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
-        """Exchange requests and rows with all_to_all; returns one hook per layer."""
-        dev_index = self.device.index if self.device.type == "cuda" else None
-        self._check_fetch_args(indices, dev_index, require_cuda=self.device.type == "cuda")
-        if self.device.type != "cuda" and indices.device.type != "cpu":
+        """Exchange requests and rows with all_to_all; returns one hook per layer.
+
+        On a CUDA device, pinned host indices are accepted like the native
+        buffer accepts them; here they are copied to the device without
+        blocking (a copy-engine H2D on the current stream).
+        """
+        on_cuda = self.device.type == "cuda"
+        dev_index = self.device.index if on_cuda else None
+        self._check_fetch_args(indices, dev_index, require_cuda=on_cuda, allow_pinned=on_cuda)
+        if not on_cuda and indices.device.type != "cpu":
             raise ValueError("indices must live on the buffer's device")
+        if on_cuda and indices.device.type == "cpu":
+            indices = indices.to(self.device, non_blocking=True)
         qps = num_qps or self.num_allocated_qps
         if not 1 <= qps <= self.num_allocated_qps:
             raise ValueError("num_qps exceeds the allocated channels")
