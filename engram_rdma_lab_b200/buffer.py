@@ -336,13 +336,14 @@ class EngramBuffer(EngramBufferBase):
         rt.set_hot_active(False)
         replica = rt.replica_view()
         bases = [sum(self.hot_rows[:l]) for l in range(c.layers)]
+        dev = replica.device  # the fill's requests live where the replica does
         with torch.cuda.device(self.device):
             for start, counts in replica_chunks(self.hot_rows, c.capacity):
-                idx = torch.full((c.layers, c.max_tokens, c.ept), -1, dtype=torch.int32, device="cuda")
+                idx = torch.full((c.layers, c.max_tokens, c.ept), -1, dtype=torch.int32, device=dev)
                 flat = idx.view(c.layers, -1)
                 for layer, n in enumerate(counts):
                     if n:
-                        flat[layer, :n] = torch.arange(start, start + n, dtype=torch.int32, device="cuda")
+                        flat[layer, :n] = torch.arange(start, start + n, dtype=torch.int32, device=dev)
                 outs = [h() for h in self.fetch(idx)]
                 for layer, n in enumerate(counts):
                     if n:

@@ -4,7 +4,9 @@ The Python orchestration (bootstrap exchange -> route probe -> agreement ->
 commit -> connect) must end the same way on every rank: when one rank's step
 fails, all ranks raise and release their runtime, and nobody waits forever in
 a later collective.  Failures are injected on the host into a stand-in for
-``_C.Runtime``; no GPU is used (gloo, world size 2).
+``_C.Runtime``; no GPU is used (gloo, world size 2).  The same stand-in,
+answering fetches from the pattern oracle, checks the order of the hot-prefix
+replica fill (off, capacity-sized fetches, health check, on) and its content.
 """
 
 import contextlib
@@ -16,6 +18,9 @@ import torch
 from ._spawn import run_ranks
 
 PHASES = ("init", "bootstrap", "probe", "prepare", "connect")
+
+
+calls = []  # data-path calls of the fake runtime in this process
 
 
 def _install_fakes(rank, world, fail_phase, fail_rank, closed, probe_errors=None):
@@ -58,6 +63,35 @@ def _install_fakes(rank, world, fail_phase, fail_rank, closed, probe_errors=None
 
         def memory_usage(self):
             return {"fake": True}
+
+        # Data path stand-ins for the replica-fill test: a "fetch" returns the
+        # pattern oracle's rows, like the kernels would.
+        def write(self, layer, storage, scales):
+            pass
+
+        def fetch(self, indices, qps, col_major):
+            from engram_rdma_lab_b200.models import expected_outputs
+
+            c = self.cfg
+            dtype = torch.bfloat16 if c["packs"] == 0 else torch.float8_e4m3fn
+            exp = expected_outputs(indices, c["entries"], c["hidden"], dtype, c["packs"])
+            calls.append(("fetch", int((indices >= 0).sum())))
+            return [e[0].view(dtype).reshape(indices.shape[1], -1) for e in exp]
+
+        def wait_layer(self, layer):
+            pass
+
+        def check_health(self):
+            calls.append(("health",))
+
+        def replica_view(self):
+            if not hasattr(self, "_replica"):
+                rows = sum(self.cfg["hot_rows"])
+                self._replica = torch.zeros(rows, self.cfg["hidden"] * self.cfg["element_bytes"], dtype=torch.uint8)
+            return self._replica
+
+        def set_hot_active(self, on):
+            calls.append(("hot", bool(on)))
 
     _native._C = types.SimpleNamespace(Runtime=FakeRuntime)
     torch.cuda.is_available = lambda: True
@@ -133,3 +167,35 @@ def _one_direction_fails(rank, world):
 
 def test_probe_failure_downgrades_only_that_pair(port):
     run_ranks(_one_direction_fails, 2, port)
+
+
+def _replica_fill(rank, world):
+    import os
+
+    from engram_rdma_lab_b200.base import EngramBufferBase
+    from engram_rdma_lab_b200.models import pattern_shard, row_pattern
+
+    os.environ["ENGRAM_EGM_ENABLE"] = "1"
+    os.environ["ENGRAM_HOT_ROWS"] = "100,37"
+    closed = []
+    _install_fakes(rank, world, None, None, closed)
+    buf, args = _make(world)  # capacity 16 tokens x 4 = 64 rows per fetch
+    buf.set_config(*args)
+    assert buf.hot_rows == [100, 37]
+    # The CPU stand-in returns CPU views; relax only the device check.
+    check = EngramBufferBase._check_fetch_args
+    buf._check_fetch_args = lambda idx, dev, **kw: check(buf, idx, None, require_cuda=False)
+    storages, _ = pattern_shard(rank, world, args[0], args[1], torch.bfloat16, 0, "cpu")
+    buf.write(storages)
+    # Off during the fill, two capacity-sized fetches (ids 0-63, 64-99 / 0-36), health check, then on.
+    assert [c for c in calls if c[0] != "fetch"] == [("hot", False), ("health",), ("hot", True)]
+    assert [c[1] for c in calls if c[0] == "fetch"] == [64 + 37, 36]
+    replica = buf.runtime.replica_view()
+    # Replica row hot_base[l] + x holds global id x of layer l (pattern rows are keyed by global id).
+    want = [row_pattern(torch.arange(hot), layer, 128) for layer, hot in enumerate(buf.hot_rows)]
+    assert torch.equal(replica, torch.cat(want))
+    os.environ.pop("ENGRAM_HOT_ROWS", None)
+
+
+def test_hot_replica_fill_orchestration(port):
+    run_ranks(_replica_fill, 2, port)
