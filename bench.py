@@ -131,6 +131,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     from engram_rdma_lab_b200.models import CONFIGS, make_indices
     from engram_rdma_lab_b200.parallel import gather_floats
+    from engram_rdma_lab_b200.utils.env import describe_knobs
     from engram_rdma_lab_b200.utils.timing import ClockSampler, L2Flusher, percentile
 
     spec = CONFIGS[args.config]
@@ -251,6 +252,7 @@ def main():
                 "parallelism": f"vocab-sharded x{world} (every rank requester and owner)",
                 "numa": NUMA,
                 "hot_rows": getattr(buf, "hot_rows", None),
+                "knobs": describe_knobs(),
                 "route": args.route if native else "all_to_all",
                 "graph": bool(args.graph),
                 "distribution": spec.distribution,

@@ -56,6 +56,7 @@ from .routing import (
     owner_routes,
     route_names,
 )
+from .utils.env import describe_knobs
 
 __all__ = ["EngramBuffer", "theoretical_config"]
 
@@ -391,6 +392,7 @@ class EngramBuffer(EngramBufferBase):
             fabric_domain=self.fabric_domain,
             fabric_probe_error=self.fabric_error,
             transport="nvlink peer loads / owner push",
+            knobs=describe_knobs(),
             memory=self.runtime.memory_usage(),
         )
 

@@ -1,4 +1,5 @@
-"""Scoped environment overrides (reference: ``deepep/deep_ep/utils/envs.py:22-37``)."""
+"""Scoped environment overrides (reference: ``deepep/deep_ep/utils/envs.py:22-37``)
+and the table of the buffer's ``ENGRAM_*`` knobs."""
 
 from __future__ import annotations
 
@@ -24,3 +25,24 @@ class EnvOverride:
             else:
                 os.environ[name] = value
         return False
+
+
+# Every environment knob the buffer reads, with its default and meaning.
+KNOBS = {
+    "ENGRAM_EGM_ENABLE": ("0", "1 = prefer the peer-HBM route (adds an HBM mirror of the shard)"),
+    "ENGRAM_WRITE_LOCAL_SF": ("= ENGRAM_EGM_ENABLE", "1 = full local FP8 scale table, 0 = each owner's rows only"),
+    "ENGRAM_DEDUP": ("auto", "move each distinct row once per fetch: auto, 1 or 0"),
+    "ENGRAM_GATHER_KERNEL": ("auto", "gather variant: auto, simt (16-B loads) or bulk (TMA ring)"),
+    "ENGRAM_GATHER_CTAS_PER_SM": ("0", "SIMT grid cap per SM (0 = 2)"),
+    "ENGRAM_GATHER_UNROLL": ("0", "SIMT row steps in flight for 256-byte rows (0 = 4)"),
+    "ENGRAM_GATHER_STRIDED": ("0", "1 = SIMT warps stride over 32-row groups instead of equal ranges"),
+    "ENGRAM_HOST_VMM": ("1", "host shards as CUDA-VMM HOST_NUMA allocations (else memfd + cudaHostRegister)"),
+    "ENGRAM_HOT_ROWS": ("", "replicate global ids [0, H) of each layer on every rank (H or H0,H1,...)"),
+    "ENGRAM_NVTX": ("0", "1 = NVTX ranges around fetch, hooks, write and owner-service launches"),
+}
+
+
+def describe_knobs(environ=None) -> dict:
+    """``{name: value}`` of every ``ENGRAM_*`` knob: the set value, or ``default:<d>``."""
+    environ = os.environ if environ is None else environ
+    return {name: environ.get(name, f"default:{default}") for name, (default, _) in KNOBS.items()}

@@ -215,3 +215,18 @@ def test_replica_fill_plan_covers_every_hot_id_once():
     for layer, hot in enumerate([250, 30, 0]):
         covered = [start + i for start, counts in plan for i in range(counts[layer])]
         assert covered == list(range(hot))
+
+
+def test_knob_table_covers_every_env_read():
+    import pathlib
+    import re
+
+    from engram_rdma_lab_b200.utils import KNOBS, describe_knobs
+
+    pkg = pathlib.Path(__file__).resolve().parents[1] / "engram_rdma_lab_b200"
+    used = set()
+    for path in pkg.rglob("*.py"):
+        used |= set(re.findall(r'"(ENGRAM_[A-Z_]+)"', path.read_text()))
+    assert used <= set(KNOBS), used - set(KNOBS)
+    got = describe_knobs({"ENGRAM_DEDUP": "0"})
+    assert got["ENGRAM_DEDUP"] == "0" and got["ENGRAM_HOT_ROWS"] == "default:"
