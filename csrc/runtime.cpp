@@ -114,6 +114,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         check(at < (1ull << 32) && sf_at < (1ull << 32), "local vocabulary too large");
         table_rows_ = at;
 
+        if (cfg.contains("index_staging"))
+            stage_indices_ = get<bool>(cfg, "index_staging");
         if (cfg.contains("nvtx") && get<bool>(cfg, "nvtx"))
             nvtx_enabled().store(true);
         py::dict plan = get<py::dict>(cfg, "plan");
@@ -178,6 +180,16 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             int lo = 0, hi = 0;
             check_cuda(cudaDeviceGetStreamPriorityRange(&lo, &hi), "stream priorities");
             check_cuda(cudaStreamCreateWithPriority(&owner_stream_, cudaStreamNonBlocking, hi), "owner stream");
+            if (stage_indices_) {
+                check_cuda(cudaStreamCreateWithFlags(&stage_stream_, cudaStreamNonBlocking), "staging stream");
+                for (int i = 0; i < 2; ++i) {
+                    check_cuda(cudaEventCreateWithFlags(&stage_copied_[i], cudaEventDisableTiming), "staging event");
+                    check_cuda(cudaEventCreateWithFlags(&stage_free_[i], cudaEventDisableTiming), "staging event");
+                    check_cuda(cudaMalloc(reinterpret_cast<void **>(&stage_buf_[i]),
+                                          std::max<size_t>(size_t(layers_) * capacity_ * 4, 16)),
+                               "staging buffer");
+                }
+            }
         } catch (...) {
             release();
             throw;
@@ -368,7 +380,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     // step's H2D happens inside the kernels that consume it, with no copy
     // engine round trip); its pinned block is recorded on the stream so the
     // host allocator does not hand it out again before they finish.
-    const int32_t *index_pointer(const torch::Tensor &indices) {
+    const int32_t *index_pointer(const torch::Tensor &indices, cudaStream_t host_user = nullptr) {
         auto stream = at::cuda::getCurrentCUDAStream(device_);
         if (indices.is_cuda()) {
             try {
@@ -389,9 +401,33 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             check(false, "host indices must be in pinned (page-locked, mapped) memory");
         }
         const auto &storage = indices.storage();
-        at::getHostAllocator(at::kCUDA)->record_event(storage.mutable_data(), storage.data_ptr().get_context(),
-                                                      stream.unwrap());
+        const c10::Stream user = host_user ? c10::Stream(at::cuda::getStreamFromExternal(host_user, device_))
+                                           : stream.unwrap();
+        at::getHostAllocator(at::kCUDA)->record_event(storage.mutable_data(), storage.data_ptr().get_context(), user);
         return static_cast<const int32_t *>(attr.devicePointer);
+    }
+
+    // Index staging (ENGRAM_INDEX_STAGING=1, eager fetches of pinned host
+    // indices): the copy engine moves them into one of two device slots on a
+    // side stream and the compute stream waits for that copy only.  When the
+    // host enqueues a step ahead, the next step's copy runs while this step's
+    // gather does, instead of the gather waiting on PCIe reads itself.  A
+    // slot is refilled only after the kernels of the fetch that read it two
+    // steps earlier (stage_free_).
+    const int32_t *stage_host_indices(const torch::Tensor &indices, cudaStream_t s, uint32_t *slot_out) {
+        index_pointer(indices, stage_stream_);  // checks pinned and ties the host block to the copy
+        const uint32_t slot = stage_next_;
+        stage_next_ ^= 1u;
+        if (stage_used_[slot])
+            check_cuda(cudaStreamWaitEvent(stage_stream_, stage_free_[slot], 0), "staging slot reuse");
+        check_cuda(cudaMemcpyAsync(stage_buf_[slot], indices.data_ptr<int32_t>(), size_t(indices.numel()) * 4,
+                                   cudaMemcpyHostToDevice, stage_stream_),
+                   "stage indices");
+        check_cuda(cudaEventRecord(stage_copied_[slot], stage_stream_), "record staged indices");
+        check_cuda(cudaStreamWaitEvent(s, stage_copied_[slot], 0), "wait for staged indices");
+        stage_used_[slot] = true;
+        *slot_out = slot;
+        return stage_buf_[slot];
     }
 
     py::list fetch(const torch::Tensor &indices, uint32_t channels, bool col_major) {
@@ -414,7 +450,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             for (uint32_t l = 0; l < layers_; ++l)
                 if (finished_stream_[l] != s)
                     check_cuda(cudaStreamWaitEvent(s, finished_[l], 0), "workspace reuse dependency");
-        const int32_t *idx = index_pointer(indices);
+        uint32_t staged_slot = 2;  // 2 = not staged
+        const int32_t *idx = (stage_indices_ && indices.is_cpu() && !issue_captured_ && indices.numel() > 0)
+                                 ? stage_host_indices(indices, s, &staged_slot)
+                                 : index_pointer(indices);
         tokens_ = uint32_t(indices.size(1));
         const uint32_t rows = tokens_ * ept_;
         uint32_t ts, hs, ls;
@@ -452,6 +491,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 ++launches_;
             }
         }
+        if (staged_slot < 2)
+            check_cuda(cudaEventRecord(stage_free_[staged_slot], s), "staging slot read");
         if (issue_captured_) {
             check_cuda(cudaEventRecord(capture_issued_, s), "record capture issue");
             check_cuda(cudaEventRecordWithFlags(issued_, s, cudaEventRecordExternal), "record external issue");
@@ -564,6 +605,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["hot_rows"] = hot_rows_;
         d["hot_replica_bytes"] = dev_replica_bytes_;
         d["hot_replica_active"] = hot_active_;
+        d["index_staging"] = stage_indices_;
         return d;
     }
 
@@ -1006,6 +1048,21 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             cudaStreamDestroy(owner_stream_);
             owner_stream_ = nullptr;
         }
+        if (stage_stream_) {
+            cudaStreamSynchronize(stage_stream_);
+            cudaStreamDestroy(stage_stream_);
+            stage_stream_ = nullptr;
+        }
+        for (int i = 0; i < 2; ++i) {
+            if (stage_copied_[i])
+                cudaEventDestroy(stage_copied_[i]);
+            if (stage_free_[i])
+                cudaEventDestroy(stage_free_[i]);
+            if (stage_buf_[i])
+                cudaFree(stage_buf_[i]);
+            stage_copied_[i] = stage_free_[i] = nullptr;
+            stage_buf_[i] = nullptr;
+        }
         if (host_error_) {
             cudaFreeHost(host_error_);
             host_error_ = nullptr;
@@ -1039,6 +1096,13 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     size_t dev_replica_ = 0, dev_replica_bytes_ = 0;
     std::vector<uint32_t> hot_rows_, hot_bases_;
     bool hot_active_ = false;
+    // index staging (see stage_host_indices)
+    bool stage_indices_ = false;
+    cudaStream_t stage_stream_ = nullptr;
+    cudaEvent_t stage_copied_[2] = {nullptr, nullptr}, stage_free_[2] = {nullptr, nullptr};
+    int32_t *stage_buf_[2] = {nullptr, nullptr};
+    uint32_t stage_next_ = 0;
+    bool stage_used_[2] = {false, false};
     uint32_t *dedup_state_ = nullptr, *dedup_stats_ = nullptr, *dedup_stats_dev_ = nullptr;
     uint32_t dedup_slots_ = 0, dedup_seen_epoch_ = 0, dedup_since_probe_ = 0;
     double dedup_ratio_ = -1.0;

@@ -239,6 +239,7 @@ class EngramBuffer(EngramBufferBase):
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),
+            index_staging=env_flag("ENGRAM_INDEX_STAGING", False),
         )
         native = None
         with torch.cuda.device(self.device):

@@ -261,9 +261,11 @@ def _pinned_view(idx, offset):
 
 @pytest.mark.parametrize("kernel", ["simt", "bulk"])
 @pytest.mark.parametrize("dedup", ["0", "1"])
-def test_pinned_host_indices_read_in_place(kernel, dedup, monkeypatch):
+@pytest.mark.parametrize("staging", ["0", "1"])
+def test_pinned_host_indices_read_in_place(kernel, dedup, staging, monkeypatch):
     monkeypatch.setenv("ENGRAM_GATHER_KERNEL", kernel)
     monkeypatch.setenv("ENGRAM_DEDUP", dedup)
+    monkeypatch.setenv("ENGRAM_INDEX_STAGING", staging)
     entries, hidden, ept, dtype, packs = (5003, 5009), 256, 24, torch.float8_e4m3fn, 2
     buf = make_buffer(entries, hidden, 512, ept, dtype, packs, True)
     try:
@@ -278,6 +280,13 @@ def test_pinned_host_indices_read_in_place(kernel, dedup, monkeypatch):
             check(outs, idx, entries, hidden, dtype, packs, col_major=col_major)
         with pytest.raises(ValueError, match="pinned host"):
             buf.fetch(idx.clone())  # pageable host memory is refused before any launch
+        assert buf.memory_usage()["index_staging"] == (staging == "1")
+        # Back-to-back fetches from rotating pinned tensors, checked after the last.
+        pool = [_pinned_view(make_indices(0, 1, entries, 512, ept, epoch=10 + k), 0) for k in range(3)]
+        for k in range(7):
+            outs = [h() for h in buf.fetch(pool[k % 3])]
+        torch.cuda.synchronize()
+        check(outs, pool[6 % 3], entries, hidden, dtype, packs)
     finally:
         buf.destroy()
 
