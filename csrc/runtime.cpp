@@ -380,7 +380,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     // step's H2D happens inside the kernels that consume it, with no copy
     // engine round trip); its pinned block is recorded on the stream so the
     // host allocator does not hand it out again before they finish.
-    const int32_t *index_pointer(const torch::Tensor &indices, cudaStream_t host_user = nullptr) {
+    const int32_t *index_pointer(const torch::Tensor &indices) {
         auto stream = at::cuda::getCurrentCUDAStream(device_);
         if (indices.is_cuda()) {
             try {
@@ -401,9 +401,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             check(false, "host indices must be in pinned (page-locked, mapped) memory");
         }
         const auto &storage = indices.storage();
-        const c10::Stream user = host_user ? c10::Stream(at::cuda::getStreamFromExternal(host_user, device_))
-                                           : stream.unwrap();
-        at::getHostAllocator(at::kCUDA)->record_event(storage.mutable_data(), storage.data_ptr().get_context(), user);
+        at::getHostAllocator(at::kCUDA)->record_event(storage.mutable_data(), storage.data_ptr().get_context(),
+                                                      stream.unwrap());
         return static_cast<const int32_t *>(attr.devicePointer);
     }
 
@@ -415,7 +414,11 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     // slot is refilled only after the kernels of the fetch that read it two
     // steps earlier (stage_free_).
     const int32_t *stage_host_indices(const torch::Tensor &indices, cudaStream_t s, uint32_t *slot_out) {
-        index_pointer(indices, stage_stream_);  // checks pinned and ties the host block to the copy
+        // Checks that the memory is pinned and ties its block to the compute
+        // stream, which outlives this runtime and waits for the copy below
+        // (torch's host allocator records an event there when the block is
+        // freed; a private stream could be gone by then).
+        index_pointer(indices);
         const uint32_t slot = stage_next_;
         stage_next_ ^= 1u;
         if (stage_used_[slot])
