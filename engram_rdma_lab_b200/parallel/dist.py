@@ -25,8 +25,12 @@ def init_dist(backend: str | None = None, timeout_s: float = 120.0, device_id: b
     """Initialise the default process group from torchrun-style env vars.
 
     Returns ``(rank, world_size, local_rank)``.  With ``backend=None`` the NCCL
-    backend is used when CUDA is available, gloo otherwise.
+    backend is used when CUDA is available, gloo otherwise.  When the default
+    group exists already, its own rank and size are returned.
     """
+    if dist.is_initialized():
+        rank, world = dist.get_rank(), dist.get_world_size()
+        return rank, world, int(os.environ.get("LOCAL_RANK", str(rank)))
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
@@ -39,8 +43,7 @@ def init_dist(backend: str | None = None, timeout_s: float = 120.0, device_id: b
         torch.cuda.set_device(local_rank)
         if device_id:
             kwargs["device_id"] = torch.device("cuda", local_rank)
-    if not dist.is_initialized():
-        dist.init_process_group(**kwargs)
+    dist.init_process_group(**kwargs)
     return rank, world, local_rank
 
 

@@ -1,0 +1,67 @@
+"""Host-side helpers: numeric utilities, scoped env overrides, the event helper's
+error paths and the process-group helpers (gloo, world size 2)."""
+
+import os
+
+import pytest
+import torch
+
+from engram_rdma_lab_b200.utils import EnvOverride, EventOverlap
+from engram_rdma_lab_b200.utils.math import align, calc_diff, ceil_div, count_bytes, hash_tensors, safe_div
+
+from ._spawn import run_ranks
+
+
+def test_math_helpers():
+    assert ceil_div(7, 2) == 4 and ceil_div(8, 2) == 4 and align(5, 4) == 8 and align(8, 4) == 8
+    assert safe_div(0, 0) == 0 and safe_div(3, 2) == 1.5
+    with pytest.raises(ZeroDivisionError):
+        safe_div(1, 0)
+    x = torch.randn(64, generator=torch.Generator().manual_seed(0))
+    assert calc_diff(x, x) == pytest.approx(0.0, abs=1e-12)
+    assert calc_diff(x, -x) > 0.1
+    assert count_bytes(torch.zeros(3, dtype=torch.float32), (torch.zeros(2, dtype=torch.int64), None)) == 28
+    a, b = torch.arange(4, dtype=torch.int32), torch.ones(2, dtype=torch.float16)
+    assert hash_tensors(a, b) == hash_tensors(b, a)
+    assert hash_tensors(a) != hash_tensors(a + 1)
+
+
+def test_env_override_restores_previous_values():
+    os.environ["ENGRAM_TEST_A"] = "old"
+    os.environ.pop("ENGRAM_TEST_B", None)
+    with EnvOverride([("ENGRAM_TEST_A", "new", True), ("ENGRAM_TEST_B", "set", True), ("ENGRAM_TEST_C", "x", False)]):
+        assert os.environ["ENGRAM_TEST_A"] == "new" and os.environ["ENGRAM_TEST_B"] == "set"
+        assert "ENGRAM_TEST_C" not in os.environ
+    assert os.environ["ENGRAM_TEST_A"] == "old" and "ENGRAM_TEST_B" not in os.environ
+    os.environ.pop("ENGRAM_TEST_A")
+
+
+def test_event_overlap_misuse_is_refused():
+    empty = EventOverlap()
+    with pytest.raises(RuntimeError):
+        empty.current_stream_wait()
+    with empty:  # leaving a context without an event waits for nothing
+        pass
+    empty.register_hook_after_wait(lambda: 1)
+    with pytest.raises(RuntimeError):
+        empty.register_hook_after_wait(lambda: 2)
+
+
+def _dist_helpers(rank, world):
+    from engram_rdma_lab_b200.parallel import gather_floats, max_over_ranks
+    from engram_rdma_lab_b200.parallel.dist import init_dist
+
+    assert init_dist(backend="gloo") == (rank, world, rank)  # already initialised: returns the placement
+    assert max_over_ranks(float(rank) * 2.5) == 2.5
+    assert gather_floats([rank, rank + 0.5]) == [[0, 0.5], [1, 1.5]]
+
+
+def test_process_group_helpers_over_gloo(port):
+    run_ranks(_dist_helpers, 2, port)
+
+
+def test_single_process_helpers_without_a_group():
+    from engram_rdma_lab_b200.parallel import gather_floats, max_over_ranks
+
+    assert max_over_ranks(3.0) == 3.0
+    assert gather_floats([1.0, 2.0]) == [[1.0, 2.0]]
