@@ -230,3 +230,20 @@ def test_knob_table_covers_every_env_read():
     assert used <= set(KNOBS), used - set(KNOBS)
     got = describe_knobs({"ENGRAM_DEDUP": "0"})
     assert got["ENGRAM_DEDUP"] == "0" and got["ENGRAM_HOT_ROWS"] == "default:"
+
+
+def test_random_init_tables():
+    from engram_rdma_lab_b200.models import normal_bf16_shard, quantized_fp8_shard
+
+    bf = normal_bf16_shard(1, 4, (300, 301), 64, "cpu")
+    assert [t.shape for t in bf] == [(300, 64), (301, 64)] and bf[0].dtype == torch.bfloat16
+    assert 0.015 < float(bf[0].float().std()) < 0.025
+    assert torch.equal(bf[0], normal_bf16_shard(1, 4, (300, 301), 64, "cpu")[0])
+    assert not torch.equal(bf[0], normal_bf16_shard(2, 4, (300, 301), 64, "cpu")[0])
+    codes0, scales0 = quantized_fp8_shard(0, 4, (300, 301), 256, 2, "cpu")
+    codes1, scales1 = quantized_fp8_shard(1, 4, (300, 301), 256, 2, "cpu")
+    assert codes0[0].dtype == torch.float8_e4m3fn and codes0[0].shape == (300, 256)
+    assert scales0[0].shape == (4 * 300, 2) and torch.equal(scales0[1], scales1[1])  # global table, same everywhere
+    assert not torch.equal(codes0[0].view(torch.uint8), codes1[0].view(torch.uint8))
+    sc = scales0[0]
+    assert float(sc.min()) >= 2**-8 and float(sc.max()) <= 1.0 and torch.all(torch.log2(sc) == torch.round(torch.log2(sc)))
