@@ -42,7 +42,7 @@ import torch.distributed as dist
 
 from . import _native
 from .base import EngramBufferBase, accept_legacy_storage_size
-from .layout import hot_rows_for, plan_memory, replica_chunks, storage_size_hint, validate_config
+from .layout import hot_rows_for, plan_memory, replica_chunks, storage_size_hint
 from .routing import (
     EgmConfig,
     OwnerRoute,

@@ -1,6 +1,5 @@
 """Route negotiation and topology helpers (host only)."""
 
-import ctypes
 
 import pytest
 
