@@ -44,6 +44,10 @@
 
 namespace py = pybind11;
 
+// Types holding Python objects get hidden visibility, like pybind11's own;
+// the module init function below is exported explicitly by PYBIND11_MODULE.
+#pragma GCC visibility push(hidden)
+
 namespace engram {
 
 enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
@@ -1188,6 +1192,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
 };
 
 } // namespace engram
+
+#pragma GCC visibility pop
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     using namespace engram;
