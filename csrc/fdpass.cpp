@@ -71,6 +71,16 @@ void FdServer::loop() {
         int conn = accept4(listen_fd_, nullptr, nullptr, SOCK_CLOEXEC);
         if (conn < 0)
             continue;
+        // Abstract socket names are visible to every local user
+        // (/proc/net/unix): hand descriptors only to processes of this
+        // user, as pidfd_getfd's ptrace check would.
+        ucred cred{};
+        socklen_t cred_len = sizeof(cred);
+        if (getsockopt(conn, SOL_SOCKET, SO_PEERCRED, &cred, &cred_len) != 0 || cred.uid != getuid()) {
+            rejected_.fetch_add(1);
+            ::close(conn);
+            continue;
+        }
         // Bounded request read: a client that never sends is dropped.
         pollfd q{conn, POLLIN, 0};
         int32_t index = -1;

@@ -4,7 +4,8 @@
 // Unix socket; an importer connects, names an index and receives a duplicate
 // through SCM_RIGHTS.  This replaces the reference's pidfd_getfd import
 // (sge_write/csrc/storage.hpp:165-178, deepep/csrc/kernels/comm/symmetric.hpp:229-252),
-// which requires ptrace permission over the exporter.
+// which requires ptrace permission over the exporter; likewise the server
+// answers only peers of its own user id (SO_PEERCRED).
 #pragma once
 
 #include <atomic>
@@ -26,6 +27,7 @@ class FdServer {
     void stop() noexcept;
     const std::string &name() const { return name_; }
     long served() const { return served_.load(); }
+    long rejected() const { return rejected_.load(); }  // connections from other users
 
   private:
     void loop();
@@ -33,7 +35,7 @@ class FdServer {
     std::vector<int> fds_;
     int listen_fd_ = -1;
     std::atomic<bool> stop_{false};
-    std::atomic<long> served_{0};
+    std::atomic<long> served_{0}, rejected_{0};
     std::thread thread_;
 };
 

@@ -116,7 +116,8 @@ void bind_harness(py::module_ &m) {
     py::class_<FdServer>(m, "FdServer")
         .def(py::init<const std::string &, std::vector<int>>())
         .def("stop", &FdServer::stop)
-        .def_property_readonly("served", &FdServer::served);
+        .def_property_readonly("served", &FdServer::served)
+        .def_property_readonly("rejected", &FdServer::rejected);
     m.def("fetch_fd", &fetch_fd, py::arg("name"), py::arg("index"), py::arg("timeout_s") = 30.0);
     m.def("memfd_with_bytes", &memfd_with_bytes);
     m.def("read_fd_bytes", &read_fd_bytes);

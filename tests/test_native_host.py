@@ -95,6 +95,35 @@ def test_fd_server_same_process():
         C.fetch_fd("engram-test-local", 0, 0.2)  # server gone
 
 
+def test_fd_server_refuses_other_users():
+    import os
+    import subprocess
+    import sys
+
+    if os.geteuid() != 0:
+        pytest.skip("switching to another user needs root")
+    fd = C.memfd_with_bytes(b"private")
+    server = C.FdServer("engram-test-uid", [fd])
+    code = (
+        "import os, socket, struct\n"
+        "s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)\n"
+        "os.setgid(65534); os.setuid(65534)\n"
+        "s.connect('\\0engram-test-uid')\n"
+        "s.sendall(struct.pack('i', 0))\n"
+        "s.settimeout(5)\n"
+        "try:\n"
+        "    print('refused' if not s.recv(16) else 'served')\n"
+        "except ConnectionResetError:\n"
+        "    print('refused')\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "refused"  # closed (or reset) without a byte or a descriptor
+    assert server.rejected == 1 and server.served == 0
+    assert C.read_fd_bytes(C.fetch_fd("engram-test-uid", 0, 5.0), 7) == b"private"  # same user still served
+    server.stop()
+
+
 def _fd_exchange(rank, world, token):
     import torch.distributed as dist
 
