@@ -149,19 +149,25 @@ class EngramBufferBase(ABC):
             raise RuntimeError("write() must initialize the vocabulary before fetch()")
         if self._pending:
             raise RuntimeError("Call every previous layer hook before the next fetch")
+        # Runs on every fetch: few tensor property reads (each costs a call
+        # into torch), one get_device() for both the device and its index.
         c = self._config
-        ok = (
-            isinstance(indices, torch.Tensor)
-            and indices.ndim == 3
-            and indices.shape[0] == c.layers
-            and indices.shape[2] == c.ept
-            and 0 <= indices.shape[1] <= c.max_tokens
-            and indices.dtype == torch.int32
-            and indices.is_contiguous()
-        )
+        ok = isinstance(indices, torch.Tensor) and indices.dim() == 3
+        if ok:
+            layers, tokens, ept = indices.shape
+            ok = (
+                layers == len(c.entries)
+                and ept == c.ept
+                and tokens <= c.max_tokens
+                and indices.dtype is torch.int32
+                and indices.is_contiguous()
+            )
         if ok and require_cuda:
-            on_device = indices.is_cuda and (device_index is None or indices.device.index == device_index)
-            ok = on_device or (allow_pinned and indices.device.type == "cpu" and indices.is_pinned())
+            device = indices.get_device()  # -1 on the CPU
+            if device < 0:
+                ok = allow_pinned and indices.device.type == "cpu" and indices.is_pinned()
+            else:
+                ok = indices.is_cuda and (device_index is None or device == device_index)
         if not ok:
             where = ("CUDA or pinned host " if allow_pinned else "CUDA ") if require_cuda else ""
             raise ValueError(
