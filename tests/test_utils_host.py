@@ -65,3 +65,16 @@ def test_single_process_helpers_without_a_group():
 
     assert max_over_ranks(3.0) == 3.0
     assert gather_floats([1.0, 2.0]) == [[1.0, 2.0]]
+
+
+def test_doctor_reports_without_a_gpu(capsys):
+    import json
+
+    from engram_rdma_lab_b200 import doctor
+
+    assert doctor.main(["--json"]) == 0  # the extension is built in-tree
+    r = json.loads(capsys.readouterr().out)
+    assert r["extension"]["loaded"] and "gather_simt_kernel" in r["extension"]["kernels"]
+    assert set(r["knobs"]) >= {"ENGRAM_EGM_ENABLE", "ENGRAM_HOT_ROWS"}
+    assert doctor.main([]) == 0
+    assert "knobs:" in capsys.readouterr().out
