@@ -63,7 +63,11 @@ def _peer_hbm(rank, world):
     _setup(rank)
     entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
     for local_sf in (False, True):
+        # First pass: the default kernel choice (the TMA ring for remote rows);
+        # second pass: 16-byte loads from the peers' mirrors.
+        os.environ["ENGRAM_GATHER_KERNEL"] = "simt" if local_sf else "auto"
         buf = _buffer(entries, hidden, 512, ept, dtype, packs, egm=True, local_sf=local_sf)
+        assert buf.memory_usage()["gather_kernel"] == ("simt" if local_sf else "tma_bulk")
         info = buf.get_route_info()
         assert info["owner_routes"] == ["peer_hbm"] * world, info
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")
@@ -92,6 +96,7 @@ def _peer_hbm(rank, world):
         del graph
         dist.barrier()
         buf.destroy()
+    os.environ.pop("ENGRAM_GATHER_KERNEL", None)
 
 
 def _host_route(rank, world):
