@@ -1,5 +1,6 @@
 // Standalone operators of the extension: the per-owner request pack (the
-// dispatch kernel aimed at caller-owned buffers) and the NVTX switch.
+// dispatch kernel aimed at caller-owned buffers), a zero-copy host read (the
+// PCIe envelope of kernels that read pinned host memory) and the NVTX switch.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <pybind11/stl.h>
@@ -80,9 +81,30 @@ void route_pack(const torch::Tensor &indices, const std::vector<uint32_t> &entri
 }
 
 
+// Streams `src` (pinned host memory, read in place through its device
+// mapping with 16-byte SM loads) into `dst` (this GPU) on the current stream.
+// Both are contiguous with the same byte size, a multiple of 16.
+void host_read(const torch::Tensor &src, torch::Tensor &dst, int blocks) {
+    check(src.is_cpu() && src.is_contiguous() && dst.is_cuda() && dst.is_contiguous() && src.nbytes() == dst.nbytes() &&
+              src.nbytes() % 16 == 0 && blocks >= 1 && blocks <= 65535,
+          "host_read: pinned contiguous source and a CUDA destination of the same size (16-byte multiple)");
+    cudaPointerAttributes attr{};
+    const bool mapped = cudaPointerGetAttributes(&attr, src.data_ptr()) == cudaSuccess &&
+                        attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr;
+    if (!mapped) {
+        cudaGetLastError();
+        check(false, "host_read: the source must be pinned (page-locked, mapped) host memory");
+    }
+    c10::cuda::CUDAGuard guard(dst.get_device());
+    cudaStream_t s = at::cuda::getCurrentCUDAStream(dst.get_device()).stream();
+    check_cuda(launch_stream_copy(attr.devicePointer, dst.data_ptr(), uint64_t(src.nbytes()), blocks, s),
+               "launch host read");
+}
+
 } // namespace
 
 void bind_ops(py::module_ &m) {
+    m.def("host_read", &host_read, py::arg("src"), py::arg("dst"), py::arg("blocks") = 592);
     m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),
           py::arg("packed"), py::arg("counts"), py::arg("scratch"));
     m.def("set_nvtx", [](bool on) { nvtx_enabled().store(on); }, py::arg("enabled"),

@@ -1,4 +1,4 @@
-"""Single-GPU ops: per-owner request packing vs. a plain torch reference."""
+"""Single-GPU ops: per-owner request packing vs. a plain torch reference, and the zero-copy host read."""
 
 import pytest
 import torch
@@ -47,3 +47,16 @@ def test_route_pack_empty_and_padding_only():
     empty = torch.empty(1, 0, 4, dtype=torch.int32, device="cuda")
     packed, counts = route_pack(empty, entries, 4)
     assert int(counts.sum()) == 0
+
+
+def test_host_read_streams_pinned_memory_into_the_gpu():
+    from engram_rdma_lab_b200 import _native
+
+    C = _native.load()
+    src = torch.randint(0, 255, (3 * 65536 + 48,), dtype=torch.uint8).pin_memory()
+    dst = torch.zeros(src.numel(), dtype=torch.uint8, device="cuda")
+    C.host_read(src, dst, 37)
+    torch.cuda.synchronize()
+    assert torch.equal(dst.cpu(), src)
+    with pytest.raises(RuntimeError, match="pinned"):
+        C.host_read(src.clone(), dst, 8)  # pageable memory is refused
