@@ -60,6 +60,8 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--with-baseline", action="store_true")
     p.add_argument("--hot-rows", default="", help="ENGRAM_HOT_ROWS for our buffer (hot-prefix replica)")
+    p.add_argument("--kernels", default="auto",
+                   help="comma-separated ENGRAM_GATHER_KERNEL values to compare for our buffer, e.g. bulk,simt")
     args = p.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -75,9 +77,12 @@ def main():
     cap = max(token_list)
     storages, scales = quantized_fp8_shard(rank, world, entries, hidden, packs, "cuda")
     flush = L2Flusher()
-    impls = [("ours", EngramBuffer)] + ([("nccl_all_to_all", TorchEngramBuffer)] if args.with_baseline else [])
+    impls = [(f"ours:{k}" if k != "auto" else "ours", EngramBuffer, k) for k in args.kernels.split(",")]
+    impls += [("nccl_all_to_all", TorchEngramBuffer, None)] if args.with_baseline else []
     group = dist.group.WORLD
-    for name, cls in impls:
+    for name, cls, kernel in impls:
+        if kernel:
+            os.environ["ENGRAM_GATHER_KERNEL"] = kernel
         sizes = cls.get_storage_size_hint(group, entries, hidden, cap, ept, dtype, packs)
         buf = cls(group, *sizes, True, 4, 1024, explicitly_destroy=True)
         buf.set_config(entries, hidden, cap, ept, dtype, packs)
