@@ -53,8 +53,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-numa-bind", action="store_true",
                    help="leave the CPU affinity alone (default: pin to the GPU's local CPUs before pinned allocations)")
-    p.add_argument("--e2e-input", choices=["pinned", "copy"], default="pinned",
-                   help="end-to-end input path: pinned host indices read by the kernels, or a copy-engine H2D")
+    p.add_argument("--e2e-input", choices=["copy", "pinned"], default="copy",
+                   help="end-to-end input path: a copy-engine H2D one step ahead on a side stream (measured faster "
+                        "on most boxes), or pinned host indices read in place by the kernels")
     p.add_argument("--no-clocks", action="store_true")
     return p.parse_args()
 
@@ -271,11 +272,11 @@ def main():
 def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
     """Same metric through the public API, with every step's input H2D and result D2H.
 
-    Step k hands ``fetch`` a pinned host index tensor (the default,
-    ``--e2e-input pinned``): the lookup kernels read the indices in place over
-    PCIe, so the step's H2D is fused into them.  ``--e2e-input copy`` instead
-    copies the indices with the copy engine into one of two device buffers on
-    a side stream, one step ahead.  Every hook runs, then token 0's rows of
+    By default (``--e2e-input copy``) step k+1's indices are copied from
+    pinned host memory by the copy engine into one of two device buffers on a
+    side stream while step k runs.  ``--e2e-input pinned`` hands ``fetch`` the
+    pinned host tensor itself, and the lookup kernels read it in place over
+    PCIe.  Every hook runs, then token 0's rows of
     the last layer are read back into pinned host memory (one D2H copy).  The
     host pool has 32 separate pinned index tensors (25 MB), cycled, so a step
     never finds its indices in a cache.  The time is one CUDA-event interval
