@@ -199,6 +199,33 @@ cudaError_t launch_expand(const DedupParams &p, int num_sms, cudaStream_t stream
 cudaError_t launch_wait_probe(const uint64_t *flag, uint64_t expected, uint64_t timeout_ns, ErrorSink error,
                               cudaStream_t stream);
 
+// Peer-memory probe (peer_probe.cu): random rows moved between this GPU and
+// its peers with one access mechanism per CTA parity (diagnostics only).
+enum ProbeMode : uint32_t {
+    kProbePullV4 = 0,      // 16-byte loads from the peer, 4 row groups in flight
+    kProbePullV4Deep = 1,  // the same with 8 row groups in flight
+    kProbePullV8 = 2,      // 32-byte loads from the peer
+    kProbePullLdgsts = 3,  // 16-byte cp.async from the peer into a shared ring
+    kProbePushV4 = 4,      // 16-byte stores into the peer
+    kProbePushV8 = 5,      // 32-byte stores into the peer
+    kProbePushBulk = 6,    // bulk copies shared -> peer global (local bulk loads feed them)
+};
+
+struct PeerProbeParams {
+    uint64_t peer_table[kMaxRanks];  // pull sources: each rank's table (this rank's own included)
+    uint64_t peer_out[kMaxRanks];    // push destinations: each rank's output region
+    const uint8_t *local_table;      // push source
+    uint8_t *local_out;              // pull destination
+    ErrorSink error;
+    uint64_t table_rows, out_rows;
+    uint32_t rows, world, rank, row_bytes;
+    uint32_t mode_even, mode_odd;    // ProbeMode of even / odd CTAs
+    uint32_t even_share_pct;         // rows taken by the even CTAs when the modes differ
+    uint32_t seed;
+};
+
+cudaError_t launch_peer_probe(const PeerProbeParams &p, int blocks, cudaStream_t stream);
+
 // Message-passing litmus test of the release/acquire flag protocol.
 enum LitmusRole : uint32_t { kLitmusProducer = 0, kLitmusConsumer = 1, kLitmusBoth = 2 };
 enum LitmusStatus : uint32_t { kLitmusProducerTimeout = 1, kLitmusConsumerTimeout = 2 };

@@ -729,6 +729,57 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         return double(ms) * 1e3;
     }
 
+    // Random-row peer probe (peer_probe.cu): `rows` rows of the agreed row size
+    // move between this GPU and pseudo-random remote peers, even CTAs with
+    // `mode_even`, odd CTAs with `mode_odd` (ProbeMode).  Pull reads the peers'
+    // HBM mirrors into this rank's output region; push reads this rank's mirror
+    // and writes the peers' output regions.  Returns the device time in
+    // microseconds.  Diagnostics only: needs the mirror (ENGRAM_EGM_ENABLE=1)
+    // and every peer on the peer-HBM route, and runs between fetches.
+    double debug_peer_probe(uint32_t mode_even, uint32_t mode_odd, uint32_t rows, int blocks, uint32_t even_share_pct,
+                            uint32_t seed) {
+        check(connected_ && !closed_ && egm_, "the probe needs a connected buffer with the HBM mirror");
+        check(mode_even <= kProbePushBulk && mode_odd <= kProbePushBulk && even_share_pct <= 100, "probe mode");
+        check(row_bytes_ % 256 == 0 && row_bytes_ <= 1024, "the probe moves rows of 256, 512 or 1024 bytes");
+        PeerProbeParams pp{};
+        const uint64_t arena = arena_->ptr();
+        for (uint32_t o = 0; o < world_; ++o) {
+            check(o == rank_ || (peer_dev_[o] && routes_[o] == kPeerHbm), "probe needs every peer on the peer-HBM route");
+            const uint64_t base = o == rank_ ? arena : peer_dev_[o]->ptr();
+            pp.peer_table[o] = base + dev_mirror_;
+            pp.peer_out[o] = base + dev_output_;
+        }
+        pp.local_table = reinterpret_cast<const uint8_t *>(arena + dev_mirror_);
+        pp.local_out = reinterpret_cast<uint8_t *>(arena + dev_output_);
+        pp.error = sink();
+        pp.table_rows = table_rows_;
+        pp.out_rows = uint64_t(layers_) * capacity_;
+        pp.rows = rows;
+        pp.world = world_;
+        pp.rank = rank_;
+        pp.row_bytes = row_bytes_;
+        pp.mode_even = mode_even;
+        pp.mode_odd = mode_odd;
+        pp.even_share_pct = even_share_pct;
+        pp.seed = seed * 0x9E3779B9u + rank_;
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, s);
+        const cudaError_t rc = launch_peer_probe(pp, blocks, s);
+        cudaEventRecord(b, s);
+        check_cuda(rc, "peer probe");
+        check_cuda(cudaEventSynchronize(b), "peer probe sync");
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        check_health();
+        return double(ms) * 1e3;
+    }
+
     // Litmus test of the release/acquire flag protocol (between fetches only;
     // it overwrites the output region).  Header words sit at the start of
     // each rank's output region, the data after 4 KiB.  reset() zeroes this
@@ -1204,7 +1255,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.attr("MAX_PUSH_TASKS") = kMaxPushTasks;
     m.attr("KERNELS") = py::make_tuple("gather_simt_kernel", "gather_bulk_kernel", "dispatch_kernel", "push_kernel",
                                        "hook_kernel", "dedup_kernel", "expand_kernel", "litmus_kernel",
-                                       "wait_probe_kernel", "stream_copy_kernel");
+                                       "wait_probe_kernel", "stream_copy_kernel", "peer_probe_kernel");
     py::class_<Runtime, std::shared_ptr<Runtime>>(m, "Runtime")
         .def(py::init<const py::dict &>())
         .def("bootstrap", &Runtime::bootstrap)
@@ -1221,6 +1272,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("run_wait_probe", &Runtime::run_wait_probe)
         .def("debug_stop_service", &Runtime::debug_stop_service)
         .def("debug_peer_copy", &Runtime::debug_peer_copy)
+        .def("debug_peer_probe", &Runtime::debug_peer_probe, py::arg("mode_even"), py::arg("mode_odd"),
+             py::arg("rows"), py::arg("blocks"), py::arg("even_share_pct") = 50, py::arg("seed") = 1)
         .def("debug_litmus_reset", &Runtime::debug_litmus_reset)
         .def("replica_view", &Runtime::replica_view)
         .def("read_layer", &Runtime::read_layer)

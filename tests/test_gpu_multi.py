@@ -1,6 +1,6 @@
 """EngramBuffer across several GPUs of one node (one process per GPU).
 
-Needs at least two GPUs; uses up to four.  The control plane is a gloo group
+Needs at least two GPUs; uses every visible GPU, up to eight (the node size).  The control plane is a gloo group
 (the data plane never touches a process group).  NVLS is not used anywhere:
 peers are reached with plain peer loads and stores.
 """
@@ -21,7 +21,7 @@ pytestmark = [
 
 
 def _world():
-    return min(4, cuda_device_count())
+    return min(8, cuda_device_count())
 
 
 def _buffer(entries, hidden, max_tokens, ept, dtype, packs, egm, local_sf=True, timeout=30, qps=None):
