@@ -11,8 +11,13 @@ traffic).
 One step = ``fetch(indices)`` plus every layer hook, i.e. the full lookup
 (issue + transfer + scales) as the reference times it.  Each timed step uses a
 fresh index tensor and the L2 is flushed (256 MiB write) between steps outside
-the timed events.  Times are CUDA events on the launching stream; the reported
-step time is the maximum over ranks.
+the timed events.  Before each step's start event a device barrier across all
+ranks (the buffer's own NVLink barrier; an NCCL all-reduce for the baseline)
+lines the GPUs up, so every rank's step runs against every other rank's
+traffic.  Times are CUDA events on the launching stream; the reported step
+time is the maximum over ranks.  The same steps without the barrier
+("free-running") are reported beside it.  Before timing, one fetch is checked
+bit-exactly against the random-init tables of every owner.
 
 Run: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
 ``torchrun --nproc-per-node N``.  ``--impl nccl`` times the torch
@@ -57,6 +62,8 @@ def parse():
                    help="end-to-end input path: a copy-engine H2D one step ahead on a side stream (measured faster "
                         "on most boxes), or pinned host indices read in place by the kernels")
     p.add_argument("--no-clocks", action="store_true")
+    p.add_argument("--no-verify", action="store_true",
+                   help="skip the bit-exact check of one fetch against the random-init tables (outside the timing)")
     return p.parse_args()
 
 
@@ -121,6 +128,53 @@ def build_buffer(args, spec, rank, world):
     return buf
 
 
+def verify_once(buf, spec, idx, world):
+    """One fetch + hooks, checked bit-exactly against every owner's random-init rows."""
+    from engram_rdma_lab_b200.models import expected_random_init
+
+    outs = [h() for h in buf.fetch(idx)]
+    torch.cuda.synchronize()
+    want = expected_random_init(idx, spec.entries, spec.hidden, spec.dtype, spec.num_sf_packs, world)
+    bad = 0
+    T = idx.shape[1]
+    for layer, out in enumerate(outs):
+        data, sf = out if spec.num_sf_packs else (out, None)
+        bad += int(data.view(torch.uint8).reshape(T, -1).ne(want[layer][0]).sum())
+        if spec.num_sf_packs:
+            bad += int(sf.ne(want[layer][1]).sum())
+    everyone = [None] * world
+    dist.all_gather_object(everyone, bad)  # every rank stops together on a mismatch
+    if any(everyone):
+        raise SystemExit(f"verification failed: values differing per rank {everyone}")
+    return True
+
+
+def timed_steps(args, steps, run, flush, align, stream, host_split):
+    """``steps`` steps, each bracketed by CUDA events; returns per-step ms on this rank."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for k in range(steps):
+        flush()
+        if align is not None:
+            align()
+        starts[k].record(stream)
+        run(k, host_split)
+        ends[k].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def summarize(step_ms, steps, bytes_req):
+    from engram_rdma_lab_b200.parallel import gather_floats
+    from engram_rdma_lab_b200.utils.timing import percentile
+
+    all_ms = gather_floats(step_ms)
+    per_step_max = [max(r[k] for r in all_ms) for k in range(steps)]
+    ms_per_step = max(sum(r) for r in all_ms) / steps
+    return dict(ms_per_step=ms_per_step, per_requester_gbs=bytes_req / (ms_per_step * 1e-3) / 1e9,
+                p50_us=statistics.median(per_step_max) * 1e3, p99_us=percentile(per_step_max, 0.99) * 1e3)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -131,9 +185,8 @@ def main():
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     from engram_rdma_lab_b200.models import CONFIGS, make_indices
-    from engram_rdma_lab_b200.parallel import gather_floats
     from engram_rdma_lab_b200.utils.env import describe_knobs
-    from engram_rdma_lab_b200.utils.timing import ClockSampler, L2Flusher, percentile
+    from engram_rdma_lab_b200.utils.timing import ClockSampler, L2Flusher
 
     spec = CONFIGS[args.config]
     if args.tokens:
@@ -148,10 +201,22 @@ def main():
     flush = L2Flusher()
     stream = torch.cuda.current_stream()
     native = args.impl == "ours"
+    verified = None if args.no_verify else verify_once(buf, spec, pool[0], world)
+    if native:
+        align = buf.device_barrier
+    else:
+        token = torch.zeros(1, device="cuda")
+        align = lambda: dist.all_reduce(token)  # noqa: E731 - an NCCL kernel every rank must reach
 
-    def step(idx):
+    def step(idx, host_split=None):
+        t0 = time.perf_counter()
         hooks = buf.fetch(idx)
-        return [h() for h in hooks]
+        t1 = time.perf_counter()
+        outs = [h() for h in hooks]
+        if host_split is not None:
+            host_split[0].append(t1 - t0)
+            host_split[1].append(time.perf_counter() - t1)
+        return outs
 
     graph, graph_idx = None, None
     if args.graph:
@@ -165,20 +230,19 @@ def main():
             step(graph_idx)
         graph_launches = (buf.runtime.memory_usage()["kernel_launches"] - before) if native else 0
 
-    def run(k):
+    def run(k, host_split=None):
         if graph is None:
-            return step(pool[k % pool_size])
+            return step(pool[k % pool_size], host_split)
         graph_idx.copy_(pool[k % pool_size])
         graph.replay()
         return None
 
     for k in range(args.warmup):
+        align()
         run(k)
     torch.cuda.synchronize()
     dist.barrier()
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches_before = buf.runtime.memory_usage()["kernel_launches"] if native else 0
     sampler = ClockSampler(gpu_index=_physical_index(local)) if not args.no_clocks else None
     if sampler:
@@ -186,29 +250,23 @@ def main():
     dist.barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
-    for k in range(args.steps):
-        flush()
-        if graph is not None:
-            graph_idx.copy_(pool[k % pool_size])
-        starts[k].record(stream)
-        if graph is None:
-            step(pool[k % pool_size])
-        else:
-            graph.replay()
-        ends[k].record(stream)
-    torch.cuda.synchronize()
+    host_split = ([], [])
+    aligned_ms = timed_steps(args, args.steps, run, flush, align, stream, host_split)
     wall = time.perf_counter() - wall0
+    launches = (buf.runtime.memory_usage()["kernel_launches"] - launches_before) if native else 0
+    dist.barrier()
+    torch.cuda.synchronize()
+    free_ms = timed_steps(args, args.steps, run, flush, None, stream, None)
     dist.barrier()
     if sampler:
         sampler.__exit__(None, None, None)
-    launches = (buf.runtime.memory_usage()["kernel_launches"] - launches_before) if native else 0
     if graph is not None:
-        launches = graph_launches * args.steps  # kernels replayed from the captured graph
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    all_ms = gather_floats(step_ms)
-    per_step_max = [max(r[k] for r in all_ms) for k in range(args.steps)]
-    rank_totals = [sum(r) for r in all_ms]
-    ms_per_step = max(rank_totals) / args.steps
+        # Kernels replayed from the captured graph, plus one barrier per step.
+        launches = (graph_launches + 1) * args.steps
+    phases = buf.phase_ms() if not native and hasattr(buf, "phase_ms") else None
+    bytes_req = spec.bytes_per_fetch(T)
+    aligned = summarize(aligned_ms, args.steps, bytes_req)
+    free = summarize(free_ms, args.steps, bytes_req)
 
     e2e = None
     if not args.no_e2e:
@@ -217,9 +275,11 @@ def main():
     clocks = sampler.summary() if sampler else {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["not sampled"]}
     all_clocks = [None] * world
     dist.all_gather_object(all_clocks, clocks)
+    host = [None] * world
+    med = (lambda v: round(statistics.median(v) * 1e6, 2) if v else None)  # noqa: E731
+    dist.all_gather_object(host, (med(host_split[0]), med(host_split[1])))
     if rank == 0:
-        bytes_req = spec.bytes_per_fetch(T)
-        per_req_gbs = bytes_req / (ms_per_step * 1e-3) / 1e9
+        per_req_gbs = aligned["per_requester_gbs"]
         reasons = sorted({r for c in all_clocks for r in (c.get("reasons") or [])})
         line = {
             "metric": METRIC,
@@ -228,16 +288,21 @@ def main():
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(ms_per_step, 5),
+            "ms_per_step": round(aligned["ms_per_step"], 5),
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(per_req_gbs / BASELINE_GBS_PER_REQUESTER, 3),
             "dtype": "fp8_e4m3" if spec.num_sf_packs else "bf16",
             "data": f"synthetic (random-init tables, seeded {spec.distribution} indices)",
             "impl": "ours" if native else "nccl_all_to_all_baseline",
+            "verified": verified,
             "per_requester_gbs": round(per_req_gbs, 3),
-            "p50_fetch_to_hook_us": round(statistics.median(per_step_max) * 1e3, 2),
-            "p99_fetch_to_hook_us": round(percentile(per_step_max, 0.99) * 1e3, 2),
+            "p50_fetch_to_hook_us": round(aligned["p50_us"], 2),
+            "p99_fetch_to_hook_us": round(aligned["p99_us"], 2),
+            "free_running": {"per_requester_gbs": round(free["per_requester_gbs"], 3),
+                             "ms_per_step": round(free["ms_per_step"], 5), "p50_fetch_to_hook_us": round(free["p50_us"], 2),
+                             "note": "same steps without the device barrier before each start event"},
+            "host_us_p50": {"fetch_call": [h[0] for h in host], "hooks_calls": [h[1] for h in host]},
             "gpu_launches": int(launches),
             "wall_s_timed_loop": round(wall, 3),
             "e2e": e2e,
@@ -258,10 +323,13 @@ def main():
                 "graph": bool(args.graph),
                 "distribution": spec.distribution,
                 "l2": "flushed between timed steps (256 MiB write + read-back outside the events); fresh indices per step",
-                "timing": "CUDA events per step on the launching stream, max over ranks",
+                "timing": "CUDA events per step on the launching stream, ranks aligned by a device barrier before "
+                          "each start event, max over ranks",
                 "baseline_gbs_per_requester": BASELINE_GBS_PER_REQUESTER,
             },
         }
+        if phases is not None:
+            line["baseline_phases_last_step"] = phases
         print(json.dumps(line), flush=True)
     buf.destroy()
     del graph

@@ -9,8 +9,9 @@ maximum over ranks:
 * ``rows``: every rank moves random 256-byte rows to or from pseudo-random
   remote peers (all-to-all, the traffic of a uniform fetch) with each access
   mechanism of ``csrc/kernels/peer_probe.cu``: 16- and 32-byte register
-  loads, 16-byte cp.async into a shared ring, 16- and 32-byte stores, and bulk
-  stores from shared memory; plus pull and push sharing one launch.
+  loads, 16-byte cp.async into a shared ring, 16- and 32-byte stores, bulk
+  stores from shared memory, stores into consecutive peer rows (a staging
+  pattern), streaming row loads; plus pull and push sharing one launch.
 
 These are the roofline denominators of the NVLink-bound kernels.
 
@@ -36,11 +37,10 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 from engram_rdma_lab_b200 import EngramBuffer  # noqa: E402
 
 MODES = {"pull_v4": 0, "pull_v4_deep": 1, "pull_v8": 2, "pull_ldgsts": 3, "push_v4": 4, "push_v8": 5,
-         "push_bulk": 6}
-ROW_CASES = [("pull_v4", "pull_v4"), ("pull_v4_deep", "pull_v4_deep"), ("pull_v8", "pull_v8"),
-             ("pull_ldgsts", "pull_ldgsts"), ("push_v4", "push_v4"), ("push_v8", "push_v8"),
-             ("push_bulk", "push_bulk"), ("pull_ldgsts", "push_bulk"), ("pull_ldgsts", "push_v4"),
-             ("pull_v4_deep", "push_v8")]
+         "push_bulk": 6, "push_seq_v8": 7, "pull_seq_v8": 8}
+ROW_CASES = [("pull_v4", "pull_v4"), ("pull_v8", "pull_v8"), ("pull_ldgsts", "pull_ldgsts"), ("push_v4", "push_v4"),
+             ("push_v8", "push_v8"), ("push_bulk", "push_bulk"), ("push_seq_v8", "push_seq_v8"),
+             ("pull_seq_v8", "pull_seq_v8"), ("pull_v8", "push_v8")]
 
 
 def parse():

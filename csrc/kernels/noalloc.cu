@@ -1,34 +1,17 @@
 // engram_route_pack_noalloc: an allocation-free entry point to the per-owner
-// request pack.
+// request pack.  The contract (what it computes, limits, set-up, sharing and
+// the callers it is for) is declared in engram_noalloc.h; this file defines it
+// against that declaration.
 //
-// This entry point has no counterpart in the reference; it exists for callers
-// that cannot allocate GPU memory on their own: code running while a stream is
-// being captured into a CUDA Graph (cudaMalloc is not allowed there), plugins
-// that run inside a host framework which owns every device allocation through
-// its own pool, and plain C callers that link this library without torch and
-// its caching allocator.  The caller passes the indices and the two outputs;
-// the kernel's scratch (per-(layer, owner) slot cursors and per-layer arrival
-// counters, plus an unused epoch block the kernel signature needs) lives in a
-// file-scope device array of fixed size, `kNoAllocScratchBytes` (32 KiB),
-// which every GPU that loads this library keeps until the process exits.
-//
-// Limits: at most 32 layers and 64 owners (the array holds exactly that);
-// larger requests are rejected with an error message and nothing runs.
-//
-// Set-up: the first call on a device (with that device current) looks up the
-// device address of the array with cudaGetSymbolAddress and caches it; make
-// that first call before any stream capture.  Host code never passes the
-// array's host-side name to a kernel, only the looked-up device address.
-//
-// Sharing: every call on a device uses the same array and it keeps the last
-// call's contents.  The entry point clears the cursors and counters on the
-// caller's stream before the kernel, so calls ordered on one stream (or
-// otherwise serialised) are correct; calls that overlap on the GPU, e.g. on
-// two unsynchronised streams, race on the array and give wrong results.
-//
-// The entry point calls no allocating routine: no cudaMalloc, no cudaFree, no
-// torch allocation; only cudaGetSymbolAddress (once per device),
-// cudaMemsetAsync on the array, and the kernel launch.
+// It has no counterpart in the reference.  Its callers cannot allocate GPU
+// memory themselves (CUDA Graph stream capture, plugins whose host framework
+// owns all device memory, C callers without torch's allocator), so the
+// dispatch kernel's scratch lives in a file-scope device array of
+// ENGRAM_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+// exit.  Host code never hands the array's host-side name to a kernel: the
+// first call on a device looks up its device address with
+// cudaGetSymbolAddress (that device current) and caches it.
+#include "engram_noalloc.h"
 #include "params.h"
 
 #include <cstdio>
@@ -37,10 +20,12 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 32 * 1024;
+constexpr size_t kNoAllocScratchBytes = ENGRAM_NOALLOC_SCRATCH_BYTES;
+static_assert(ENGRAM_NOALLOC_MAX_LAYERS == engram::kMaxLayers && ENGRAM_NOALLOC_MAX_OWNERS == engram::kMaxRanks,
+              "header limits follow the kernel's tables");
 constexpr int kNoAllocMaxDevices = 64;
 
-// cursors [32 x 64] u32 (8 KiB) | arrivals [32] u32 | epochs [32 x 64] u64 (16 KiB)
+// cursors [32 x 64] u32 (8 KiB) | arrivals [32] u32 | epochs [32 x 64] u64 (16 KiB, at 16 KiB)
 static __device__ __align__(256) unsigned char g_route_pack_scratch[kNoAllocScratchBytes];
 
 std::mutex g_setup_mutex;
@@ -78,13 +63,6 @@ void *scratch_for_current_device(char *err, size_t err_len) {
 
 } // namespace
 
-// Packs the non-padding requests of `indices` ([layers, tokens * ept] int32 on
-// the current device) per owner, exactly as the route_pack op does:
-//   packed[o][l][i] = (position << 32) | (table_base[l] + x % entries[l])
-// for i < counts[l][o], where owner o = x / entries[l] and owners_host[o] != 0.
-// `packed` is int64 [world][layers][capacity], `counts` int32 [layers][world];
-// `entries_host` and `owners_host` are host arrays of length layers / world.
-// Returns 0 on success; otherwise a nonzero code and a message in `err`.
 extern "C" int engram_route_pack_noalloc(const int32_t *indices, uint32_t layers, uint32_t tokens, uint32_t ept,
                                          const uint32_t *entries_host, uint32_t world, const uint8_t *owners_host,
                                          int64_t *packed, uint32_t capacity, int32_t *counts, cudaStream_t stream,
@@ -94,21 +72,21 @@ extern "C" int engram_route_pack_noalloc(const int32_t *indices, uint32_t layers
         set_message(err, err_len,
                     "engram_route_pack_noalloc: layers must be in [1, 32] and world in [1, 64] "
                     "(the fixed scratch array holds no more)");
-        return 1;
+        return ENGRAM_NOALLOC_BAD_SHAPE;
     }
     const uint64_t rows = uint64_t(tokens) * ept;
     if (rows > capacity || rows * layers >= (1ull << 32)) {
         set_message(err, err_len, "engram_route_pack_noalloc: tokens * ept exceeds capacity or 32-bit indexing");
-        return 2;
+        return ENGRAM_NOALLOC_BAD_ROWS;
     }
     if ((rows > 0 && indices == nullptr) || packed == nullptr || counts == nullptr || entries_host == nullptr ||
         owners_host == nullptr) {
         set_message(err, err_len, "engram_route_pack_noalloc: null pointer argument");
-        return 3;
+        return ENGRAM_NOALLOC_NULL_ARG;
     }
     unsigned char *scratch = static_cast<unsigned char *>(scratch_for_current_device(err, err_len));
     if (scratch == nullptr)
-        return 4;
+        return ENGRAM_NOALLOC_NO_DEVICE;
 
     const size_t lw = size_t(kMaxLayers) * kMaxRanks;
     DispatchParams d{};
@@ -117,14 +95,20 @@ extern "C" int engram_route_pack_noalloc(const int32_t *indices, uint32_t layers
     d.epochs = reinterpret_cast<uint64_t *>(scratch + 16 * 1024);
     d.totals = reinterpret_cast<uint32_t *>(counts);
     d.error = ErrorSink{nullptr, nullptr};
-    uint32_t at = 0;
+    // Table bases are 32-bit in the packed entries: the running sum is kept in
+    // 64 bits and rejected before it could wrap.
+    uint64_t at = 0;
     for (uint32_t l = 0; l < layers; ++l) {
         if (entries_host[l] == 0 || uint64_t(entries_host[l]) * world > 0x7FFFFFFFull) {
             set_message(err, err_len, "engram_route_pack_noalloc: entries must be positive and world*entries < 2^31");
-            return 5;
+            return ENGRAM_NOALLOC_BAD_ENTRIES;
+        }
+        if (at + entries_host[l] > 0xFFFFFFFFull) {
+            set_message(err, err_len, "engram_route_pack_noalloc: the sum of entries over layers exceeds 2^32 - 1");
+            return ENGRAM_NOALLOC_BAD_ENTRIES;
         }
         d.layer.entries[l] = entries_host[l];
-        d.layer.table_bases[l] = at;
+        d.layer.table_bases[l] = uint32_t(at);
         at += entries_host[l];
     }
     for (uint32_t o = 0; o < world; ++o)
@@ -150,7 +134,7 @@ extern "C" int engram_route_pack_noalloc(const int32_t *indices, uint32_t layers
         char text[256];
         std::snprintf(text, sizeof(text), "engram_route_pack_noalloc: %s", cudaGetErrorString(rc));
         set_message(err, err_len, text);
-        return 6;
+        return ENGRAM_NOALLOC_CUDA_ERROR;
     }
     return 0;
 }

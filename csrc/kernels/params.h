@@ -40,6 +40,7 @@ enum ErrorCode : uint32_t {
     kInboxOverflow = 3,    // a request list exceeded the inbox slot
     kPushBounds = 4,       // an owner got a row id or position out of bounds
     kPipelineTimeout = 5,  // a shared-memory pipeline barrier never completed
+    kBarrierTimeout = 6,   // a peer never reached the device barrier
 };
 
 constexpr uint32_t kGatherBulk = 0;  // TMA bulk-copy ring (default)
@@ -185,11 +186,22 @@ struct HookParams {
     uint64_t timeout_ns;
 };
 
+// Bounded device barrier over NVLink (barrier.cu): one warp per GPU.
+struct BarrierParams {
+    uint64_t *count;                  // this rank's barrier count (arena scratch)
+    const uint64_t *slots;            // this rank's arrival slots [world]; peer p writes slot p
+    uint64_t peer_slot[kMaxRanks];    // address of slot[rank] in each rank's arena (own included)
+    ErrorSink error;
+    uint32_t world, rank;
+    uint64_t timeout_ns;
+};
+
 // Host launchers (defined in the .cu files).
 cudaError_t launch_gather(const GatherParams &p, int num_sms, cudaStream_t stream);
 cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream);
 cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream);
 cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream);
+cudaError_t launch_barrier(const BarrierParams &p, cudaStream_t stream);
 // 16-byte streaming copy (peer-bandwidth diagnostics).
 cudaError_t launch_stream_copy(const void *src, void *dst, uint64_t bytes, int blocks, cudaStream_t stream);
 // Request deduplication around the gather (dedup.cu).
@@ -209,6 +221,8 @@ enum ProbeMode : uint32_t {
     kProbePushV4 = 4,      // 16-byte stores into the peer
     kProbePushV8 = 5,      // 32-byte stores into the peer
     kProbePushBulk = 6,    // bulk copies shared -> peer global (local bulk loads feed them)
+    kProbePushSeqV8 = 7,   // 32-byte stores of random local rows into consecutive peer rows
+    kProbePullSeqV8 = 8,   // 32-byte loads of consecutive peer rows into consecutive local rows
 };
 
 struct PeerProbeParams {

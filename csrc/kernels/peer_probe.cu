@@ -17,6 +17,9 @@
 //                       bulk-store each row into the peer's output
 //                       (cp.async.bulk shared -> global; a store, never a load,
 //                       touches peer memory)
+//   push_seq_v8         32-byte stores of random local rows into consecutive
+//                       rows of each peer's output (a staging-buffer pattern)
+//   pull_seq_v8         32-byte loads of consecutive peer rows (streaming)
 // Even CTAs run `mode_even`, odd CTAs `mode_odd`, so one launch can also
 // measure pull and push sharing the links.  Diagnostics only: it overwrites
 // output regions and runs between fetches.  No reference counterpart.
@@ -46,9 +49,26 @@ struct RowPlan {
     uint8_t *dst;
 };
 
-__device__ __forceinline__ RowPlan plan_row(const PeerProbeParams &p, uint32_t i, bool push) {
+__device__ __forceinline__ RowPlan plan_row(const PeerProbeParams &p, uint32_t i, bool push, bool seq = false) {
     const uint32_t h = mix32(i * 2654435761u + p.seed);
     uint32_t peer = p.rank;
+    if (seq) {
+        // Row i goes to (or comes from) peer i % (world - 1) at its row
+        // i / (world - 1): consecutive rows per peer, every peer busy.
+        const uint32_t others = p.world > 1 ? p.world - 1 : 1;
+        const uint32_t q = i / others;
+        if (p.world > 1)
+            peer = (p.rank + 1 + i % others) % p.world;
+        RowPlan r;
+        if (push) {
+            r.src = p.local_table + uint64_t(mix32(h ^ 0x9E3779B9u) % p.table_rows) * p.row_bytes;
+            r.dst = reinterpret_cast<uint8_t *>(p.peer_out[peer]) + uint64_t(q % p.out_rows) * p.row_bytes;
+        } else {
+            r.src = reinterpret_cast<const uint8_t *>(p.peer_table[peer]) + uint64_t(q % p.table_rows) * p.row_bytes;
+            r.dst = p.local_out + uint64_t(i % p.out_rows) * p.row_bytes;
+        }
+        return r;
+    }
     if (p.world > 1)
         peer = (p.rank + 1 + h % (p.world - 1)) % p.world;
     const uint64_t trow = mix32(h ^ 0x9E3779B9u) % p.table_rows;
@@ -86,7 +106,8 @@ __device__ __forceinline__ void st_v8(void *ptr, const Vec32 &r) {
 // Register path: LPR lanes per row, BYTES per lane per access, UNROLL row
 // groups in flight per lane.
 template <int BYTES, int UNROLL>
-__device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint32_t hi, uint32_t warp, uint32_t warps) {
+__device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint32_t hi, uint32_t warp, uint32_t warps,
+                         bool seq = false) {
     const uint32_t lane = threadIdx.x % 32;
     const uint32_t lpr = min(32u, p.row_bytes / BYTES);
     const uint32_t rps = 32 / lpr;  // rows per warp access
@@ -97,7 +118,7 @@ __device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint3
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {
             const uint32_t i = base + u * rps + sub;
-            rp[u] = i < hi && sub < rps ? plan_row(p, i, push) : RowPlan{nullptr, nullptr};
+            rp[u] = i < hi && sub < rps ? plan_row(p, i, push, seq) : RowPlan{nullptr, nullptr};
         }
         for (uint32_t c = 0; c < per_lane; ++c) {
             const uint32_t off = (c * lpr + vl) * BYTES;
@@ -278,6 +299,12 @@ __global__ void __launch_bounds__(kProbeThreads) peer_probe_kernel(const __grid_
         break;
     case kProbePushBulk:
         ok = run_push_bulk(p, ring, bars, lo, hi, warp, warps);
+        break;
+    case kProbePushSeqV8:
+        run_regs<32, 4>(p, true, lo, hi, warp, warps, true);
+        break;
+    case kProbePullSeqV8:
+        run_regs<32, 4>(p, false, lo, hi, warp, warps, true);
         break;
     default:
         break;

@@ -547,6 +547,47 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         finished_stream_[layer] = hook_captured ? nullptr : s;
     }
 
+    // Device barrier over every rank of the buffer, enqueued on the current
+    // stream (capturable: the count lives in device memory).  Work the stream
+    // enqueued before it is visible to every peer's work enqueued after
+    // theirs.  Bounded by the buffer's GPU timeout; a timeout is reported
+    // like any device error.
+    void barrier() {
+        check_health();
+        check(connected_ && !closed_, "runtime is not connected");
+        BarrierParams b{};
+        const uint64_t own = arena_->ptr();
+        for (uint32_t o = 0; o < world_; ++o) {
+            const uint64_t base = o == rank_ ? own : peer_dev_[o]->ptr();
+            b.peer_slot[o] = base + barrier_slots_offset_ + uint64_t(rank_) * 8;
+        }
+        b.count = barrier_count_;
+        b.slots = reinterpret_cast<const uint64_t *>(own + barrier_slots_offset_);
+        b.error = sink();
+        b.world = world_;
+        b.rank = rank_;
+        b.timeout_ns = timeout_ns_;
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(launch_barrier(b, at::cuda::getCurrentCUDAStream(device_).stream()), "launch barrier");
+        ++launches_;
+    }
+
+    // Synchronous snapshot of the barrier count and slots (tests only).
+    py::dict barrier_state() {
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaDeviceSynchronize(), "barrier state sync");
+        uint64_t count = 0;
+        std::vector<uint64_t> slots(world_);
+        check_cuda(cudaMemcpy(&count, barrier_count_, 8, cudaMemcpyDeviceToHost), "read barrier count");
+        check_cuda(cudaMemcpy(slots.data(), reinterpret_cast<void *>(arena_->ptr() + barrier_slots_offset_),
+                              size_t(world_) * 8, cudaMemcpyDeviceToHost),
+                   "read barrier slots");
+        py::dict d;
+        d["count"] = count;
+        d["slots"] = slots;
+        return d;
+    }
+
     // ------------------------------------------------------------- inspection
     void check_health() {
         service_.check();
@@ -739,7 +780,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     double debug_peer_probe(uint32_t mode_even, uint32_t mode_odd, uint32_t rows, int blocks, uint32_t even_share_pct,
                             uint32_t seed) {
         check(connected_ && !closed_ && egm_, "the probe needs a connected buffer with the HBM mirror");
-        check(mode_even <= kProbePushBulk && mode_odd <= kProbePushBulk && even_share_pct <= 100, "probe mode");
+        check(mode_even <= kProbePullSeqV8 && mode_odd <= kProbePullSeqV8 && even_share_pct <= 100, "probe mode");
         check(row_bytes_ % 256 == 0 && row_bytes_ <= 1024, "the probe moves rows of 256, 512 or 1024 bytes");
         PeerProbeParams pp{};
         const uint64_t arena = arena_->ptr();
@@ -921,6 +962,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         board_ = reinterpret_cast<uint64_t *>(take(lw * 8));
         dev_error_ = reinterpret_cast<ErrorRecord *>(take(sizeof(ErrorRecord)));
         dedup_state_ = reinterpret_cast<uint32_t *>(take(16));
+        barrier_count_ = reinterpret_cast<uint64_t *>(take(8));
+        barrier_slots_offset_ = size_t(reinterpret_cast<uint8_t *>(take(size_t(world_) * 8)) -
+                                       reinterpret_cast<uint8_t *>(arena_->ptr()));
         check(at <= dev_scratch_bytes_, "scratch region too small");
     }
 
@@ -1206,6 +1250,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t *epochs_ = nullptr;
     uint32_t *totals_ = nullptr, *cursors_ = nullptr, *layer_arrivals_ = nullptr;
     uint64_t *claim_ = nullptr, *finish_ = nullptr, *board_ = nullptr;
+    // device barrier: this rank's count and the arena offset of the slots
+    // every peer writes (the same offset on every rank: the plan is agreed)
+    uint64_t *barrier_count_ = nullptr;
+    size_t barrier_slots_offset_ = 0;
     ErrorRecord *dev_error_ = nullptr, *host_error_ = nullptr, *host_error_dev_ = nullptr;
     // routes
     std::vector<int> routes_;
@@ -1233,9 +1281,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     std::string describe_error() const {
         volatile ErrorRecord *e = host_error_;
         static const char *names[] = {"ok", "hook wait timed out", "index outside the vocabulary",
-                                      "inbox overflow", "push bounds", "gather pipeline stalled"};
+                                      "inbox overflow", "push bounds", "gather pipeline stalled",
+                                      "device barrier timed out"};
         const uint32_t s = e->status;
-        std::string what = s < 6 ? names[s] : "unknown error";
+        std::string what = s < 7 ? names[s] : "unknown error";
         return "Engram device error: " + what + " (layer " + std::to_string(e->layer) + ", owner " +
                std::to_string(e->owner) + ", observed " + std::to_string(e->observed) + ", expected " +
                std::to_string(e->expected) + ", reports " + std::to_string(e->count) + ")";
@@ -1255,7 +1304,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.attr("MAX_PUSH_TASKS") = kMaxPushTasks;
     m.attr("KERNELS") = py::make_tuple("gather_simt_kernel", "gather_bulk_kernel", "dispatch_kernel", "push_kernel",
                                        "hook_kernel", "dedup_kernel", "expand_kernel", "litmus_kernel",
-                                       "wait_probe_kernel", "stream_copy_kernel", "peer_probe_kernel");
+                                       "wait_probe_kernel", "stream_copy_kernel", "peer_probe_kernel",
+                                       "barrier_kernel");
     py::class_<Runtime, std::shared_ptr<Runtime>>(m, "Runtime")
         .def(py::init<const py::dict &>())
         .def("bootstrap", &Runtime::bootstrap)
@@ -1266,6 +1316,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("fetch", &Runtime::fetch)
         .def("wait_layer", &Runtime::wait_layer)
         .def("check_health", &Runtime::check_health)
+        .def("barrier", &Runtime::barrier)
+        .def("barrier_state", &Runtime::barrier_state)
         .def("error_state", &Runtime::error_state)
         .def("memory_usage", &Runtime::memory_usage)
         .def("debug_state", &Runtime::debug_state)

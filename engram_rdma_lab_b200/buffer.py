@@ -382,6 +382,21 @@ class EngramBuffer(EngramBufferBase):
         self._input = indices
         return self._make_hooks(generation, self.runtime.wait_layer, outputs)
 
+    def device_barrier(self):
+        """Enqueue a device barrier over every rank of the group on the current stream.
+
+        One warp per GPU stores its barrier count into every peer's arena and
+        waits (bounded by ``num_gpu_timeout_secs``) until every peer's count
+        arrived; work each rank enqueued before it is visible to every rank's
+        work after it.  Every rank must call it the same number of times.  It
+        can be captured into a CUDA graph (the counts live in device memory).
+        A timeout is reported like any device error and leaves the barrier
+        unusable until the buffer is rebuilt.  Reference: the NVLink barrier
+        of ``deepep/deep_ep/include/deep_ep/comm/barrier.cuh:88-131``.
+        """
+        self._ready()
+        self.runtime.barrier()
+
     # -------------------------------------------------------------- inspection
     def get_route_info(self):
         self._ready()

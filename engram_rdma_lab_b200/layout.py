@@ -21,6 +21,8 @@ with ``capacity = max_tokens * ept`` (reference ``runtime.cpp:151-156, 519-522``
 
 from __future__ import annotations
 
+from .utils.math import align, ceil_div  # noqa: F401 - ceil_div is part of this module's helpers
+
 from dataclasses import dataclass, field
 
 import torch
@@ -32,12 +34,6 @@ MAX_RANKS = 64
 MAX_LAYERS = 32
 
 
-def align(n: int, a: int) -> int:
-    return (n + a - 1) // a * a
-
-
-def ceil_div(a: int, b: int) -> int:
-    return (a + b - 1) // b
 
 
 @dataclass(frozen=True)
@@ -179,8 +175,9 @@ def plan_memory(config: EngramConfig, world: int, mirror: bool, local_sf: bool, 
         # dedup: keys[H] u64 + vals[H] u64 + slots[L * capacity] u32
         ("dedup", (dedup_table_slots(c) * 16 + L * c.capacity * 4) if dedup else 0),
         # scratch: epochs[L*W] u64, totals[L*W] u32, cursors[L*W] u32, layer_arrivals[L] u32,
-        # serve claim/finish/board [W*L] u64 each, device error record, alignment slack
-        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 16 + 256),
+        # serve claim/finish/board [W*L] u64 each, device error record, dedup state,
+        # device barrier count u64 + slots[W] u64, alignment slack
+        ("scratch", L * W * 8 + L * W * 4 + L * W * 4 + L * 4 + 3 * W * L * 8 + 16 + 8 + W * 8 + 256),
         ("replica", sum(hot_rows or ()) * c.row_bytes),
     ]
     off = 0

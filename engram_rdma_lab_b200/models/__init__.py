@@ -2,6 +2,7 @@ from .engram_tables import (
     CONFIGS,
     TableSpec,
     expected_outputs,
+    expected_random_init,
     make_indices,
     normal_bf16_shard,
     pattern_scales,
@@ -14,6 +15,7 @@ __all__ = [
     "CONFIGS",
     "TableSpec",
     "expected_outputs",
+    "expected_random_init",
     "make_indices",
     "normal_bf16_shard",
     "pattern_scales",

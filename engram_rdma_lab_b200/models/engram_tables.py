@@ -175,6 +175,40 @@ def quantized_fp8_shard(rank: int, world: int, entries, hidden: int, packs: int,
     return storages, scales
 
 
+def expected_random_init(indices: torch.Tensor, spec_entries, hidden: int, dtype, packs: int, world: int,
+                         seed: int = 1):
+    """What a fetch of ``indices`` must return when every rank wrote the random-init tables.
+
+    The tables are :func:`quantized_fp8_shard` (``packs > 0``) or
+    :func:`normal_bf16_shard` with ``seed``; each owner's rows are regenerated
+    here from its rank (one owner at a time, so memory stays at one shard), and
+    the requested rows are gathered from them.  Returns per layer
+    ``(bytes [tokens, ept*row_bytes], scales [tokens, ept*packs] | None)`` on
+    the indices' device, like :func:`expected_outputs`.
+    """
+    device = indices.device
+    L, T, E = indices.shape
+    esize = torch.empty((), dtype=dtype).element_size()
+    row_bytes = hidden * esize
+    x = indices.reshape(L, T * E).to(torch.int64)
+    data = [torch.zeros(T * E, row_bytes, dtype=torch.uint8, device=device) for _ in range(L)]
+    scales = [None] * L
+    for owner in range(world):
+        if packs:
+            storages, sf = quantized_fp8_shard(owner, world, spec_entries, hidden, packs, device, seed)
+        else:
+            storages, sf = normal_bf16_shard(owner, world, spec_entries, hidden, device, seed=seed), None
+        for layer, n in enumerate(spec_entries):
+            mine = ((x[layer] >= 0) & (x[layer] // n == owner)).nonzero().flatten()
+            rows = storages[layer].view(torch.uint8).reshape(n, row_bytes)
+            data[layer].index_copy_(0, mine, rows.index_select(0, x[layer].index_select(0, mine) - owner * n))
+            if packs and scales[layer] is None:
+                valid = (x[layer] >= 0)[:, None].to(torch.float32)
+                scales[layer] = (sf[layer].index_select(0, x[layer].clamp_min(0)) * valid).reshape(T, E * packs)
+        del storages, sf
+    return [(d.reshape(T, E * row_bytes), scales[layer]) for layer, d in enumerate(data)]
+
+
 def _zipf_cdf(size: int, s: float, device) -> torch.Tensor:
     ranks = torch.arange(1, size + 1, dtype=torch.float64, device=device)
     w = ranks.pow(-s)

@@ -5,8 +5,9 @@ granularity of one scale pack).  A block's scale is ``amax / 448`` (448 is the
 largest finite e4m3 value), optionally rounded up to a power of two so that
 dequantisation is exact in binary floating point (the UE8M0 convention).  The
 codes are ``round_to_e4m3(x / scale)``; dequantisation multiplies back.
+``calc_diff`` measures how far a dequantised table is from its source.
 Parity: ``deepep/deep_ep/utils/math.py:30-56`` (``per_token_cast_to_fp8`` /
-``per_token_cast_back``), rewritten without ``torch.compile``.
+``per_token_cast_back``, ``calc_diff``), rewritten without ``torch.compile``.
 """
 
 from __future__ import annotations
@@ -42,3 +43,13 @@ def dequantize_fp8_blockwise(codes: torch.Tensor, scales: torch.Tensor, block: i
     padded = torch.nn.functional.pad(codes.float(), (0, blocks * block - n)).view(m, blocks, block)
     out = padded * scales.float().reshape(m, blocks, 1)
     return out.view(m, blocks * block)[:, :n].to(dtype)
+
+
+def calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
+    """Dissimilarity of ``x`` and ``y``: 1 - 2<x', y'> / (|x'|^2 + |y'|^2) with x' = x + 1, y' = y + 1.
+
+    0 means identical; a blockwise FP8 round trip of N(0, 1) data stays below 1e-3.
+    """
+    x, y = x.double() + 1, y.double() + 1
+    denominator = (x * x + y * y).sum()
+    return float((1 - 2 * (x * y).sum() / denominator).item())

@@ -3,18 +3,20 @@
 Same public API as :class:`engram_rdma_lab_b200.EngramBuffer`, built only from
 torch tensor ops and ``torch.distributed`` collectives:
 
-1. bucket every requested row by owner (``x // n_l``), padding last;
+1. bucket every requested row by owner (``x // n_l``) with a counting
+   placement, padding last;
 2. ``all_to_all_single`` of per-owner counts, then of ``(layer, local_row)``
    requests;
-3. each owner gathers the requested rows and FP8 scales from its shard;
-4. ``all_to_all_single`` of rows and scales back;
+3. each owner gathers the requested rows and FP8 scales from its shard into
+   one payload per row;
+4. one ``all_to_all_single`` of those payloads back;
 5. scatter into the per-layer output region; padding rows and scales are zero.
 
 On CPU with a ``gloo`` group it is the oracle of the unit tests.  On GPUs with
 an ``nccl`` group it is the "NCCL all_to_all" baseline the fused kernels are
 measured against.  The baseline has to read the counts back to the host to size
-the exchange, so every fetch synchronises the host once; the native buffer never
-does.  Reference semantics reproduced: ``sge_write/engram_sge_write/buffer.py``
+the exchange, so every fetch synchronises the host once (one read of the sent
+and received counts); the native buffer never does.  Reference semantics reproduced: ``sge_write/engram_sge_write/buffer.py``
 (API, validation, hook generations), ``sge_write/csrc/runtime.cpp:389-535``
 (storage, scale sharding, output and scale layouts).
 """
@@ -127,6 +129,8 @@ class TorchEngramBuffer(EngramBufferBase):
         self._sf_output = torch.zeros(max(plan.device["sf_output"][1] // 4, 1), dtype=torch.float32, device=dev)
         self.routes = [OwnerRoute.PEER_HBM if self.egm.enabled else OwnerRoute.HOST] * self.num_ranks
         self.owner_fallback_reasons = [""] * self.num_ranks
+        self._marks = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if dev.type == "cuda" else None
+        self._last_exchange = None
         self._configured = True
         dist.barrier(group=self.group)
 
@@ -183,65 +187,129 @@ class TorchEngramBuffer(EngramBufferBase):
         return self._make_hooks(generation, lambda layer: None, outputs)
 
     def _exchange(self, indices, col_major):
+        """One fetch as three ``all_to_all_single`` calls with a single host sync.
+
+        1. Bucket the requests by owner with a counting placement: a one-hot
+           running count gives each request its slot inside its owner's
+           bucket, so no sort runs.
+        2. Exchange the per-owner counts (device), then read sent and received
+           counts back together: the only host sync, needed to size the
+           variable splits.
+        3. Exchange the ``(layer << 32) | local_row`` requests.
+        4. Each owner gathers rows (``index_select``) and appends the FP8
+           scale words to each row, so one exchange returns both.
+        5. The requester scatters rows and scales to their positions with
+           ``index_copy_``; padding stays zero.
+
+        On a CUDA device every phase is bracketed by events; ``phase_ms()``
+        reads them (it synchronises) to separate the row exchange from the
+        bookkeeping around it.
+        """
         c, W, dev = self._config, self.num_ranks, self.device
         L, T, E = indices.shape
         P, R = c.num_sf_packs, c.row_bytes
         rows = T * E
-        x = indices.reshape(L, rows).to(torch.int64)
+        N = L * rows
+        marks = self._marks if dev.type == "cuda" else None
+        if marks is not None:
+            marks[0].record()
+        x = indices.reshape(N).to(torch.int64)
+        layer = torch.arange(N, device=dev, dtype=torch.int64) // max(rows, 1)
+        n = self._entries_t.index_select(0, layer)
         valid = x >= 0
-        n = self._entries_t[:, None]
         owner = torch.where(valid, torch.div(x.clamp_min(0), n, rounding_mode="floor"), torch.full_like(x, W))
-        if bool((owner[valid] >= W).any()) if valid.any() else False:
-            raise ValueError("index outside the global vocabulary")
-        local = torch.where(valid, x.clamp_min(0) % n, torch.zeros_like(x))
-        layer_ids = torch.arange(L, device=dev, dtype=torch.int64)[:, None].expand(L, rows)
-        positions = torch.arange(L * rows, device=dev, dtype=torch.int64)
-        owner_f, local_f, layer_f = owner.reshape(-1), local.reshape(-1), layer_ids.reshape(-1)
-        order = torch.sort(owner_f, stable=True).indices
-        send_counts = torch.bincount(owner_f, minlength=W + 1)[:W]
-        total = int(send_counts.sum())  # host sync: the baseline must size its buffers
-        keep = order[:total]
-        request = (layer_f[keep] << 32) | local_f[keep]
+        bad = (owner > W) | (valid & (owner >= W))
+        owner = owner.clamp_max(W)  # padding (and ids past the vocabulary) go to bucket W, never sent
+        counts = torch.bincount(owner, minlength=W + 1)
+        offsets = torch.cumsum(counts, 0) - counts
+        running = torch.nn.functional.one_hot(owner, W + 1).cumsum(0)
+        slot = offsets.index_select(0, owner) + running.gather(1, owner[:, None]).squeeze(1) - 1
+        request = torch.empty(N, dtype=torch.int64, device=dev)
+        request.index_copy_(0, slot, (layer << 32) | torch.where(valid, x.clamp_min(0) % n, torch.zeros_like(x)))
+        position_of_slot = torch.empty(N, dtype=torch.int64, device=dev)
+        position_of_slot.index_copy_(0, slot, torch.arange(N, device=dev, dtype=torch.int64))
+        send_counts = counts[:W].contiguous()
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        send_split, recv_split = send_counts.tolist(), recv_counts.tolist()
+        meta = torch.cat([send_counts, recv_counts, bad.sum().view(1)]).tolist()  # the one host sync
+        send_split, recv_split = meta[:W], meta[W:2 * W]
+        if meta[-1]:
+            raise ValueError("index outside the global vocabulary")
+        total = sum(send_split)
+        if marks is not None:
+            marks[1].record()
         incoming = torch.empty(sum(recv_split), dtype=torch.int64, device=dev)
-        dist.all_to_all_single(incoming, request, recv_split, send_split, group=self.group)
+        dist.all_to_all_single(incoming, request[:total], recv_split, send_split, group=self.group)
+        if marks is not None:
+            marks[2].record()
 
-        # Owner side: serve rows and scales from this rank's shard.
+        # Owner side: rows (and scale words) of this rank's shard, one payload per request.
         in_layer, in_row = incoming >> 32, incoming & 0xFFFFFFFF
-        served = self._table[self._table_bases[in_layer] + in_row]
-        answer = torch.empty(total, R, dtype=torch.uint8, device=dev)
-        dist.all_to_all_single(answer, served.contiguous(), send_split, recv_split, group=self.group)
+        served = self._table.index_select(0, self._table_bases.index_select(0, in_layer) + in_row)
         if P:
-            sf_off = self._entries_t[in_layer] * self.rank_idx if self.local_sf else torch.zeros_like(in_row)
-            served_sf = self._sf_table[self._sf_bases[in_layer] + sf_off + in_row]
-            answer_sf = torch.empty(total, P, dtype=torch.float32, device=dev)
-            dist.all_to_all_single(answer_sf, served_sf.contiguous(), send_split, recv_split, group=self.group)
+            sf_off = self._entries_t.index_select(0, in_layer) * self.rank_idx if self.local_sf else 0
+            sf_at = self._sf_bases.index_select(0, in_layer) + sf_off + in_row
+            served_sf = self._sf_table.index_select(0, sf_at)[:, :P].contiguous().view(torch.uint8)
+            served = torch.cat([served, served_sf], dim=1)
+        answer = torch.empty(total, served.shape[1], dtype=torch.uint8, device=dev)
+        if marks is not None:
+            marks[3].record()
+        dist.all_to_all_single(answer, served, send_split, recv_split, group=self.group)
+        if marks is not None:
+            marks[4].record()
 
         # Requester side: scatter into the output region; padding stays zero.
-        out = self._output[:, :rows]
-        out.zero_()
-        flat_out = self._output.view(L * c.capacity, R)
-        dst = (positions[keep] // rows) * c.capacity + positions[keep] % rows
-        flat_out[dst] = answer
+        positions = position_of_slot[:total]
+        dst = (positions // max(rows, 1)) * c.capacity + positions % max(rows, 1)
+        self._output[:, :rows].zero_()
+        self._output.view(L * c.capacity, R).index_copy_(0, dst, answer[:, :R])
         results = []
-        dtype = c.dtype
         if P:
             ts, hs, ls = sf_strides(T, E, P, col_major)
-            sf_rows = torch.zeros(L * rows, P, dtype=torch.float32, device=dev)
-            sf_rows[positions[keep]] = answer_sf
-            for layer in range(L):
-                view = self._sf_output.as_strided((T, E * P), (ts, hs), layer * ls)
-                view.copy_(sf_rows[layer * rows:(layer + 1) * rows].reshape(T, E * P))
-        for layer in range(L):
-            data = self._output[layer, :rows].view(dtype).reshape(T, E * c.hidden)
+            sf_rows = torch.zeros(N, P, dtype=torch.float32, device=dev)
+            sf_rows.index_copy_(0, positions, answer[:, R:].contiguous().view(torch.float32))
+            for lyr in range(L):
+                view = self._sf_output.as_strided((T, E * P), (ts, hs), lyr * ls)
+                view.copy_(sf_rows[lyr * rows:(lyr + 1) * rows].reshape(T, E * P))
+        for lyr in range(L):
+            data = self._output[lyr, :rows].view(c.dtype).reshape(T, E * c.hidden)
             if P:
                 ts, hs, ls = sf_strides(T, E, P, col_major)
-                results.append((data, self._sf_output.as_strided((T, E * P), (ts, hs), layer * ls)))
+                results.append((data, self._sf_output.as_strided((T, E * P), (ts, hs), lyr * ls)))
             else:
                 results.append(data)
+        if marks is not None:
+            marks[5].record()
+            self._last_exchange = dict(rows_sent=total, payload_bytes=int(served.shape[1]))
         return results
+
+    def phase_ms(self):
+        """Device time of the last fetch's phases (CUDA only; synchronises).
+
+        ``bookkeeping_ms``: bucketing, the count exchange and its host read;
+        ``requests_ms``: the request exchange; ``serve_ms``: the owner's row
+        and scale gather; ``rows_all_to_all_ms``: the row + scale exchange;
+        ``scatter_ms``: placing rows and scales at their positions.
+        ``rows_all_to_all_gbs``: payload bytes this rank received over that
+        exchange's time.
+        """
+        if self.device.type != "cuda" or self._last_exchange is None:
+            return None
+        m = self._marks
+        m[5].synchronize()
+        spans = [m[i].elapsed_time(m[i + 1]) for i in range(5)]
+        names = ["bookkeeping_ms", "requests_ms", "serve_ms", "rows_all_to_all_ms", "scatter_ms"]
+        out = {k: round(v, 4) for k, v in zip(names, spans)}
+        received = self._last_exchange["rows_sent"] * self._last_exchange["payload_bytes"]
+        out["rows_all_to_all_gbs"] = round(received / (spans[3] * 1e-3) / 1e9, 2) if spans[3] > 0 else None
+        out["payload_bytes_per_row"] = self._last_exchange["payload_bytes"]
+        return out
+
+    def device_barrier(self):
+        """A barrier ordered on the current stream: an all-reduce of one word over the group."""
+        self._ready()
+        token = torch.zeros(1, device=self.device)
+        dist.all_reduce(token, group=self.group)
 
     # -------------------------------------------------------------- inspection
     def get_route_info(self):

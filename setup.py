@@ -25,7 +25,7 @@ NVCC_FLAGS = [
 CXX_FLAGS = ["-O3", "-std=c++17", "-Wno-deprecated-declarations", "-Wno-interference-size"]
 
 sources = [os.path.join("csrc", f) for f in ("runtime.cpp", "memory.cpp", "fdpass.cpp", "owner_service.cpp", "harness.cpp", "ops.cpp")]
-sources += [os.path.join("csrc", "kernels", f) for f in ("gather.cu", "exchange.cu", "dedup.cu", "noalloc.cu", "litmus.cu", "peer_probe.cu")]
+sources += [os.path.join("csrc", "kernels", f) for f in ("gather.cu", "exchange.cu", "dedup.cu", "noalloc.cu", "litmus.cu", "peer_probe.cu", "barrier.cu")]
 
 setup(
     name="engram_rdma_lab_b200",

@@ -311,6 +311,51 @@ def _litmus(rank, world):
     buf.destroy()
 
 
+def _device_barrier(rank, world):
+    _setup(rank)
+    buf = _buffer((4099, 4111), 256, 64, 4, torch.bfloat16, 0, egm=True, timeout=1.0)
+    for _ in range(200):  # back to back: the counts stay in step without resets
+        buf.device_barrier()
+    state = buf.runtime.barrier_state()
+    assert state["count"] == 200 and state["slots"] == [200] * world, state
+    # A late rank holds everyone: rank 0 sleeps on its stream before arriving.
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if rank == 0:
+        torch.cuda._sleep(100_000_000)  # ~50 ms of GPU cycles
+    start.record()
+    buf.device_barrier()
+    end.record()
+    torch.cuda.synchronize()
+    if rank != 0:
+        assert start.elapsed_time(end) > 10.0, start.elapsed_time(end)
+    # Captured into a graph: each replay advances the counts.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        buf.device_barrier()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    assert buf.runtime.barrier_state()["count"] == 204
+    assert buf.error_state()["status"] == 0
+    # A rank whose peers never arrive gives up after the bounded wait.
+    dist.barrier()
+    if rank == 0:
+        buf.device_barrier()
+        torch.cuda.synchronize()
+        state = buf.error_state()
+        assert state["status"] == 6 and state["expected"] == 205, state
+        with pytest.raises(RuntimeError, match="barrier"):
+            buf.device_barrier()
+    dist.barrier()
+    buf.destroy()
+
+
+def test_device_barrier(port):
+    run_ranks(_device_barrier, _world(), port)
+
+
 def test_flag_protocol_litmus_two_gpus(port):
     run_ranks(_litmus, 2, port)
 

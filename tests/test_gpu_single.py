@@ -382,3 +382,24 @@ def test_state_dict_roundtrip_native(local_sf):
         check(outs, idx, entries, hidden, dtype, packs, salt=11)
     finally:
         fresh.destroy()
+
+
+def test_device_barrier_one_rank_and_probe():
+    """The device barrier on one rank (its own slot only), and the random-row probe on the local mirror."""
+    buf = make_buffer((4099, 4111), 256, 64, 4, torch.bfloat16, 0, True)
+    try:
+        for _ in range(10):
+            buf.device_barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            buf.device_barrier()
+        graph.replay()
+        torch.cuda.synchronize()
+        del graph
+        assert buf.runtime.barrier_state() == {"count": 11, "slots": [11]}
+        for mode in range(9):  # every ProbeMode, local rows only at world size 1
+            us = buf.runtime.debug_peer_probe(mode, mode, 4096, 148)
+            assert us > 0
+        assert buf.error_state()["status"] == 0
+    finally:
+        buf.destroy()

@@ -247,3 +247,33 @@ def test_random_init_tables():
     assert not torch.equal(codes0[0].view(torch.uint8), codes1[0].view(torch.uint8))
     sc = scales0[0]
     assert float(sc.min()) >= 2**-8 and float(sc.max()) <= 1.0 and torch.all(torch.log2(sc) == torch.round(torch.log2(sc)))
+
+
+@pytest.mark.parametrize("packs", [0, 2])
+def test_expected_random_init_matches_the_owners_tables(packs):
+    from engram_rdma_lab_b200.models import (expected_random_init, make_indices, normal_bf16_shard,
+                                             quantized_fp8_shard)
+
+    world, entries, hidden, ept, tokens = 3, (101, 67), 256, 5, 9
+    dtype = torch.float8_e4m3fn if packs else torch.bfloat16
+    idx = make_indices(1, world, entries, tokens, ept, epoch=4, padding=0.2)
+    got = expected_random_init(idx, entries, hidden, dtype, packs, world)
+    for layer, n in enumerate(entries):
+        want_rows, want_sf = [], []
+        for x in idx[layer].reshape(-1).tolist():
+            if x < 0:
+                want_rows.append(torch.zeros(hidden * dtype.itemsize, dtype=torch.uint8))
+                want_sf.append(torch.zeros(packs))
+                continue
+            owner = x // n
+            if packs:
+                storages, sf = quantized_fp8_shard(owner, world, entries, hidden, packs, "cpu")
+                want_sf.append(sf[layer][x])
+            else:
+                storages = normal_bf16_shard(owner, world, entries, hidden, "cpu")
+            want_rows.append(storages[layer][x - owner * n].view(torch.uint8))
+        assert torch.equal(got[layer][0], torch.stack(want_rows).reshape(tokens, -1))
+        if packs:
+            assert torch.equal(got[layer][1], torch.stack(want_sf).reshape(tokens, ept * packs))
+        else:
+            assert got[layer][1] is None
