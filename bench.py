@@ -58,9 +58,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-numa-bind", action="store_true",
                    help="leave the CPU affinity alone (default: pin to the GPU's local CPUs before pinned allocations)")
-    p.add_argument("--e2e-input", choices=["copy", "pinned"], default="copy",
-                   help="end-to-end input path: a copy-engine H2D one step ahead on a side stream (measured faster "
-                        "on most boxes), or pinned host indices read in place by the kernels")
+    p.add_argument("--e2e-input", choices=["copy", "staged", "pinned"], default="copy",
+                   help="end-to-end input path: a copy-engine H2D one step ahead on a side stream, the runtime's own "
+                        "staging of pinned host indices, or pinned host indices read in place by the kernels")
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--no-verify", action="store_true",
                    help="skip the bit-exact check of one fetch against the random-init tables (outside the timing)")
@@ -111,6 +111,8 @@ def build_buffer(args, spec, rank, world):
 
     os.environ["ENGRAM_EGM_ENABLE"] = "1" if args.route == "peer_hbm" else "0"
     os.environ.setdefault("ENGRAM_WRITE_LOCAL_SF", "1")
+    if args.e2e_input == "staged" and not args.no_e2e:
+        os.environ["ENGRAM_INDEX_STAGING"] = "1"
     cls = EngramBuffer if args.impl == "ours" else TorchEngramBuffer
     group = dist.group.WORLD
     sizes = cls.get_storage_size_hint(group, spec.entries, spec.hidden, spec.max_tokens, spec.ept, spec.dtype,
@@ -340,36 +342,52 @@ def main():
 def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
     """Same metric through the public API, with every step's input H2D and result D2H.
 
-    By default (``--e2e-input copy``) step k+1's indices are copied from
-    pinned host memory by the copy engine into one of two device buffers on a
-    side stream while step k runs.  ``--e2e-input pinned`` hands ``fetch`` the
-    pinned host tensor itself, and the lookup kernels read it in place over
-    PCIe.  Every hook runs, then token 0's rows of
-    the last layer are read back into pinned host memory (one D2H copy).  The
-    host pool has 32 separate pinned index tensors (25 MB), cycled, so a step
-    never finds its indices in a cache.  The time is one CUDA-event interval
-    around all steps (max over ranks); no L2 flush runs inside it, and every
-    step reads fresh random rows from a table larger than the L2.
+    Every step hands ``fetch_all`` (fetch plus every layer's wait, one native
+    call) the step's indices from pinned host memory, then reads token 0's rows
+    of the last layer back into pinned host memory (one D2H copy).  Input paths
+    (``--e2e-input``):
+
+    * ``copy``: step k+1's indices are copied by the copy engine into one of
+      two device buffers on a side stream while step k runs;
+    * ``staged``: ``fetch_all`` gets the pinned tensor and the runtime copies
+      it on its own side stream into one of two device slots
+      (``ENGRAM_INDEX_STAGING=1``, set before the buffer is built);
+    * ``pinned``: ``fetch_all`` gets the pinned tensor and the lookup kernels
+      read it in place over PCIe.
+
+    The host pool has 32 separate pinned index tensors (25 MB), cycled, so a
+    step never finds its indices in a cache.  The time is one CUDA-event
+    interval around all steps (max over ranks); no L2 flush runs inside it, and
+    every step reads fresh random rows from a table larger than the L2.  The
+    host time per step and the time of one index H2D alone are reported beside
+    it, to show which of them bounds the loop.
     """
     compute = torch.cuda.current_stream()
     base = [p.cpu() for p in pool]
     host_pool = [base[i % len(base)].clone().pin_memory() for i in range(32)]
     out_host = torch.empty(spec.ept * spec.row_bytes, dtype=torch.uint8).pin_memory()
     packs = spec.num_sf_packs
-    pinned = args.e2e_input == "pinned"
+    mode = args.e2e_input
     copier = torch.cuda.Stream()
     dev = [torch.empty_like(pool[0]), torch.empty_like(pool[0])]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     consumed = [torch.cuda.Event(), torch.cuda.Event()]
+    readback = {}
 
     def read_back(outs):
-        data = outs[-1][0] if packs else outs[-1]
-        if data.shape[0]:
-            out_host.copy_(data[0].view(torch.uint8), non_blocking=True)
+        # The runtime hands out the same output views every step: slice once.
+        key = id(outs[-1])
+        if key not in readback:
+            data = outs[-1][0] if packs else outs[-1]
+            readback.clear()
+            readback[key] = data[0].view(torch.uint8) if data.shape[0] else None
+        src = readback[key]
+        if src is not None:
+            out_host.copy_(src, non_blocking=True)
 
-    def run_pinned(steps):
+    def run_host(steps):
         for k in range(steps):
-            read_back([h() for h in buf.fetch(host_pool[k % len(host_pool)])])
+            read_back(buf.fetch_all(host_pool[k % len(host_pool)]))
 
     def run_copy(steps):
         with torch.cuda.stream(copier):
@@ -384,26 +402,40 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
                     dev[nxt].copy_(host_pool[(k + 1) % len(host_pool)], non_blocking=True)
                     ready[nxt].record(copier)
             compute.wait_event(ready[slot])
-            outs = [h() for h in buf.fetch(dev[slot])]
+            outs = buf.fetch_all(dev[slot])
             consumed[slot].record(compute)
             read_back(outs)
 
-    run = run_pinned if pinned else run_copy
+    run = run_copy if mode == "copy" else run_host
     run(args.warmup)
     torch.cuda.synchronize()
     dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
     start.record(compute)
     run(args.steps)
     end.record(compute)
+    host_s = time.perf_counter() - t0
     torch.cuda.synchronize()
     from engram_rdma_lab_b200.parallel import max_over_ranks
 
     ms_per_step = max_over_ranks(start.elapsed_time(end) / args.steps)
+    host_us = max_over_ranks(host_s / args.steps * 1e6)
+    # One index H2D alone, on an idle stream (the copy engine's share of a step).
+    h2d = []
+    for k in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(compute)
+        dev[0].copy_(host_pool[k], non_blocking=True)
+        b.record(compute)
+        torch.cuda.synchronize()
+        h2d.append(a.elapsed_time(b) * 1e3)
+    h2d_us = max_over_ranks(statistics.median(h2d))
     bytes_req = spec.bytes_per_fetch(pool[0].shape[1])
     per_req = bytes_req / (ms_per_step * 1e-3) / 1e9
-    how = ("fetch(pinned host indices): the lookup kernels read them over PCIe" if pinned else
-           "pinned H2D of the indices by the copy engine, double-buffered on a side stream")
+    how = {"copy": "pinned H2D of the indices by the copy engine, double-buffered on a side stream",
+           "staged": "fetch_all(pinned host indices): the runtime copies them to a device slot on its side stream",
+           "pinned": "fetch_all(pinned host indices): the lookup kernels read them in place over PCIe"}[mode]
     return {
         "value": round(per_req * world, 3),
         "unit": "GB/s (sum over requesters)",
@@ -411,7 +443,11 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
         "ms_per_step": round(ms_per_step, 5),
         "h2d_bytes_per_step": int(pool[0].numel() * pool[0].element_size()),
         "d2h_bytes_per_step": int(out_host.numel()),
-        "path": f"per step: {how} -> every hook -> D2H of the last layer's token-0 rows; eager public API",
+        "input_path": mode,
+        "host_us_per_step": round(host_us, 2),
+        "index_h2d_alone_us": round(h2d_us, 2),
+        "path": f"per step: {how} -> fetch_all (fetch + every layer's wait) -> D2H of the last layer's token-0 "
+                f"rows; eager public API",
         "l2": "not flushed inside the interval; 32 separate pinned index tensors cycled; fresh random rows "
               "from a table larger than L2 every step",
     }

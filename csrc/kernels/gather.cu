@@ -254,8 +254,9 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 // 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
 // per-row integer work is done by one lane instead of LPR lanes.  The next
 // kIndexAhead steps' indices are loaded before this step's rows, hiding that latency.
-template <int LPR, int VPL, int UNROLL>
+template <int LPR, int VPL, int UNROLL, int VB = 16>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
+    using V = RowVec<VB>;
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ int32_t s_index[kSimtThreads / 32][kIndexAhead * 32];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     constexpr uint32_t kMaxPacksInFlight = 4;
     const uint32_t lane = threadIdx.x % 32;
     const uint32_t sub = lane / LPR, vlane = lane % LPR;
-    const uint32_t vectors = p.row_bytes / 16;
+    const uint32_t vectors = p.row_bytes / VB;
     const uint32_t total = p.layers * p.rows;
     const uint32_t warp_id = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const uint32_t warps = gridDim.x * (blockDim.x / 32);
@@ -377,15 +378,15 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                     rs[u] = rd[u] = 0;
             }
             for (uint32_t chunk = 0; chunk < vectors; chunk += LPR * VPL) {
-                Vec16 buf[UNROLL][VPL];
+                typename V::T buf[UNROLL][VPL];
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
 #pragma unroll
                     for (int k = 0; k < VPL; ++k) {
                         const uint32_t v = chunk + vlane + k * LPR;
-                        buf[u][k] = Vec16{0, 0, 0, 0};
+                        buf[u][k] = V::zero();
                         if (rs[u] != 0 && v < vectors)
-                            buf[u][k] = ld_nc_na_v4(reinterpret_cast<const uint8_t *>(rs[u]) + uint64_t(v) * 16);
+                            buf[u][k] = V::load(reinterpret_cast<const uint8_t *>(rs[u]) + uint64_t(v) * VB);
                     }
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
                     for (int k = 0; k < VPL; ++k) {
                         const uint32_t v = chunk + vlane + k * LPR;
                         if (rd[u] != 0 && v < vectors)
-                            st_v4(reinterpret_cast<uint8_t *>(rd[u]) + uint64_t(v) * 16, buf[u][k]);
+                            V::store(reinterpret_cast<uint8_t *>(rd[u]) + uint64_t(v) * VB, buf[u][k]);
                     }
             }
         }
@@ -408,7 +409,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     }
 }
 
-template <int LPR, int VPL, int UNROLL>
+template <int LPR, int VPL, int UNROLL, int VB = 16>
 cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t total = p.layers * p.rows;
     const uint32_t groups = (total + 31) / 32;
@@ -418,12 +419,21 @@ cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream)
     blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
         return cudaSuccess;
-    gather_simt_kernel<LPR, VPL, UNROLL><<<blocks, kSimtThreads, 0, stream>>>(p);
+    gather_simt_kernel<LPR, VPL, UNROLL, VB><<<blocks, kSimtThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t vectors = p.row_bytes / 16;
+    // 256-bit vectors: 32-byte multiples of 128 bytes and more (8 lanes per
+    // 256-byte row); the 16-byte kernels serve every other row size.
+    if (p.vector_bytes == 32 && p.row_bytes % 32 == 0 && vectors >= 8) {
+        if (vectors <= 16)
+            return launch_simt<8, 1, 4, 32>(p, num_sms, stream);
+        if (vectors <= 32)
+            return launch_simt<16, 1, 4, 32>(p, num_sms, stream);
+        return launch_simt<32, 1, 4, 32>(p, num_sms, stream);
+    }
     if (vectors <= 2)
         return launch_simt<2, 1, 4>(p, num_sms, stream);
     if (vectors <= 4)

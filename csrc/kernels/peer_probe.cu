@@ -84,25 +84,6 @@ __device__ __forceinline__ RowPlan plan_row(const PeerProbeParams &p, uint32_t i
     return r;
 }
 
-struct alignas(32) Vec32 {
-    uint32_t v[8];
-};
-
-__device__ __forceinline__ Vec32 ld_nc_v8(const void *ptr) {
-    Vec32 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
-                   "=r"(r.v[7])
-                 : "l"(ptr));
-    return r;
-}
-
-__device__ __forceinline__ void st_v8(void *ptr, const Vec32 &r) {
-    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(ptr), "r"(r.v[0]), "r"(r.v[1]),
-                 "r"(r.v[2]), "r"(r.v[3]), "r"(r.v[4]), "r"(r.v[5]), "r"(r.v[6]), "r"(r.v[7])
-                 : "memory");
-}
-
 // Register path: LPR lanes per row, BYTES per lane per access, UNROLL row
 // groups in flight per lane.
 template <int BYTES, int UNROLL>
@@ -137,7 +118,7 @@ __device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint3
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
                     if (rp[u].src)
-                        v[u] = ld_nc_v8(rp[u].src + off);
+                        v[u] = ld_nc_na_v8(rp[u].src + off);
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
                     if (rp[u].src)

@@ -19,6 +19,11 @@ struct alignas(16) Vec16 {
     uint32_t x, y, z, w;
 };
 
+// 32-byte vector (sm_100 256-bit loads and stores).
+struct alignas(32) Vec32 {
+    uint32_t v[8];
+};
+
 // 16-byte read-only load that bypasses L1 allocation; the table rows are read
 // once per fetch and must not evict the caller's working set from L1.
 __device__ __forceinline__ Vec16 ld_nc_na_v4(const void *ptr) {
@@ -28,6 +33,42 @@ __device__ __forceinline__ Vec16 ld_nc_na_v4(const void *ptr) {
                  : "l"(ptr));
     return v;
 }
+
+// 32-byte read-only load without L1 allocation: one request per 32-byte
+// sector.  Over NVLink, 8 lanes x 32 B per 256-byte row moved random rows
+// ~5% faster than 16 lanes x 16 B (benchmarks/peer_bandwidth.py, rows family).
+__device__ __forceinline__ Vec32 ld_nc_na_v8(const void *ptr) {
+    Vec32 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
+                   "=r"(r.v[7])
+                 : "l"(ptr));
+    return r;
+}
+
+__device__ __forceinline__ void st_v8(void *ptr, const Vec32 &r) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(ptr), "r"(r.v[0]), "r"(r.v[1]),
+                 "r"(r.v[2]), "r"(r.v[3]), "r"(r.v[4]), "r"(r.v[5]), "r"(r.v[6]), "r"(r.v[7])
+                 : "memory");
+}
+
+// Width-generic row-vector helpers for the gather kernels.
+template <int BYTES> struct RowVec;
+template <> struct RowVec<16> {
+    using T = Vec16;
+    static __device__ __forceinline__ T zero() { return Vec16{0, 0, 0, 0}; }
+    static __device__ __forceinline__ T load(const void *p) { return ld_nc_na_v4(p); }
+    static __device__ __forceinline__ void store(void *p, const T &v) {
+        asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+    }
+};
+template <> struct RowVec<32> {
+    using T = Vec32;
+    static __device__ __forceinline__ T zero() { return Vec32{{0, 0, 0, 0, 0, 0, 0, 0}}; }
+    static __device__ __forceinline__ T load(const void *p) { return ld_nc_na_v8(p); }
+    static __device__ __forceinline__ void store(void *p, const T &v) { st_v8(p, v); }
+};
 
 // Plain 16-byte load for memory another agent may be writing concurrently
 // (host shards under a rewrite are quiesced by write(), so .nc is safe there

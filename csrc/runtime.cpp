@@ -98,6 +98,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
         if (cfg.contains("gather_strided"))
             tuning_strided_ = get<uint32_t>(cfg, "gather_strided");
+        if (cfg.contains("gather_vector"))
+            tuning_vector_ = get<uint32_t>(cfg, "gather_vector");
+        check(tuning_vector_ == 16 || tuning_vector_ == 32, "gather vector bytes must be 16 or 32");
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
         capacity_ = max_tokens_ * ept_;
@@ -515,6 +518,17 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         return py::list(cached_outputs_);
     }
 
+    // fetch() followed by wait_layer() of every layer on the same stream, in
+    // one call: for callers that consume every layer at once, the host cost
+    // of the per-layer hooks (one Python call and two stream queries each)
+    // drops out.  Returns the same output views as fetch().
+    py::list fetch_all(const torch::Tensor &indices, uint32_t channels, bool col_major) {
+        py::list outputs = fetch(indices, channels, col_major);
+        for (uint32_t l = 0; l < layers_; ++l)
+            wait_layer(l);
+        return outputs;
+    }
+
     void wait_layer(uint32_t layer) {
         TraceRange trace("engram/hook");
         check_health();
@@ -647,6 +661,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["kernel_launches"] = launches_;
         d["num_sms"] = num_sms_;
         d["gather_kernel"] = gather_variant_ == kGatherSimt ? "simt" : "tma_bulk";
+        d["gather_vector_bytes"] = tuning_vector_;
         d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
         d["dedup_fetches"] = dedup_fetches_;
         d["dedup_last_unique_ratio"] = dedup_ratio_;
@@ -819,6 +834,108 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         cudaEventDestroy(b);
         check_health();
         return double(ms) * 1e3;
+    }
+
+    // Host-route serving on one GPU (diagnostics and single-GPU profiling):
+    // this rank files a request to itself for `rows` pseudo-random rows of
+    // layer 0 and one worker serves it through the host route's own code: the
+    // push kernel ("push", `blocks` CTAs, the owner service's launch) or a hook
+    // kernel that serves while it waits for its own done flag ("hook").  Rows
+    // are read zero-copy from the pinned host shard and stored at their output
+    // positions.  Returns the device time, the bytes moved and the rows whose
+    // bytes differ from the shard.  Uses the [layer 0][this rank] slots of the
+    // serving words, which the fetch path never uses for the rank itself.
+    py::dict debug_serve_local(uint32_t rows, const std::string &worker, int blocks) {
+        check(connected_ && !closed_, "runtime is not connected");
+        check(worker == "push" || worker == "hook", "worker must be 'push' or 'hook'");
+        check(rows >= 1 && rows <= capacity_ && entries_[0] >= 1, "rows must be in [1, capacity]");
+        c10::cuda::CUDAGuard guard(device_);
+        check_cuda(cudaDeviceSynchronize(), "serve_local sync");
+        const uint32_t slot = rank_ * layers_;          // [requester = rank][layer 0]
+        const uint32_t done_slot = 0 * world_ + rank_;  // done[layer 0][owner = rank]
+        uint64_t epoch = 0;
+        check_cuda(cudaMemcpy(&epoch, claim_ + slot, 8, cudaMemcpyDeviceToHost), "read claim word");
+        epoch = (epoch >> 32) + 1;  // the claim word holds (next epoch - 1) << 32 once re-armed
+        const uint64_t armed = (epoch - 1) << 32;
+        std::vector<uint64_t> entries(rows);
+        std::vector<uint32_t> local_rows(rows);
+        uint64_t h = 0x9E3779B97F4A7C15ull ^ (uint64_t(rows) << 17) ^ epoch;
+        for (uint32_t i = 0; i < rows; ++i) {
+            h ^= h >> 31;
+            h *= 0xBF58476D1CE4E5B9ull;
+            h ^= h >> 29;
+            local_rows[i] = uint32_t(h % entries_[0]);  // layer 0 rows start at table base 0
+            entries[i] = (uint64_t(i) << 32) | local_rows[i];
+        }
+        uint64_t *inbox = reinterpret_cast<uint64_t *>(arena_->ptr() + dev_inbox_) + uint64_t(slot) * capacity_;
+        uint64_t *done = reinterpret_cast<uint64_t *>(arena_->ptr() + dev_done_) + done_slot;
+        const uint32_t total = rows;
+        check_cuda(cudaMemcpy(inbox, entries.data(), size_t(rows) * 8, cudaMemcpyHostToDevice), "fill inbox");
+        check_cuda(cudaMemcpy(claim_ + slot, &armed, 8, cudaMemcpyHostToDevice), "arm claim");
+        check_cuda(cudaMemcpy(finish_ + slot, &armed, 8, cudaMemcpyHostToDevice), "arm finish");
+        check_cuda(cudaMemcpy(totals_ + done_slot, &total, 4, cudaMemcpyHostToDevice), "request total");
+        check_cuda(cudaMemcpy(epochs_ + done_slot, &epoch, 8, cudaMemcpyHostToDevice), "request epoch");
+        check_cuda(cudaMemset(reinterpret_cast<uint8_t *>(arena_->ptr() + dev_output_), 0,
+                              size_t(rows) * row_bytes_), "clear output rows");
+        auto *header = reinterpret_cast<MailboxHeader *>(mailbox_->host_ptr()) + slot;
+        header->rows = rows;
+        header->layer = 0;
+        header->requester = rank_;
+        header->channels = channels_;
+        __atomic_store_n(&header->ready, epoch, __ATOMIC_RELEASE);
+        ServeParams v = serve_params_;
+        v.out_base[rank_] = arena_->ptr() + dev_output_;
+        v.done_base[rank_] = arena_->ptr() + dev_done_;
+        v.serve_mask = 1ull << rank_;
+        cudaStream_t s = at::cuda::getCurrentCUDAStream(device_).stream();
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, s);
+        cudaError_t rc;
+        if (worker == "push") {
+            PushParams pp{};
+            pp.s = v;
+            pp.tasks[0] = PushTask{rank_, 0, rows, channels_, epoch};
+            pp.num_tasks = 1;
+            rc = launch_push(pp, blocks, s);
+        } else {
+            HookParams hp{};
+            hp.s = v;
+            hp.totals = totals_;
+            hp.epochs = epochs_;
+            hp.done = reinterpret_cast<const uint64_t *>(arena_->ptr() + dev_done_);
+            hp.layer = 0;
+            hp.serve = 1;
+            hp.timeout_ns = timeout_ns_;
+            rc = launch_hook_wait(hp, s);
+        }
+        cudaEventRecord(b, s);
+        check_cuda(rc, "serve_local launch");
+        check_cuda(cudaEventSynchronize(b), "serve_local wait");
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        uint64_t seen = 0;
+        check_cuda(cudaMemcpy(&seen, done, 8, cudaMemcpyDeviceToHost), "read done");
+        std::vector<uint8_t> out(size_t(rows) * row_bytes_);
+        check_cuda(cudaMemcpy(out.data(), reinterpret_cast<void *>(arena_->ptr() + dev_output_), out.size(),
+                              cudaMemcpyDeviceToHost),
+                   "read output rows");
+        const uint8_t *table = static_cast<const uint8_t *>(host_->host_ptr());
+        uint64_t bad = 0;
+        for (uint32_t i = 0; i < rows; ++i)
+            bad += std::memcmp(out.data() + size_t(i) * row_bytes_, table + size_t(local_rows[i]) * row_bytes_,
+                               row_bytes_) != 0;
+        check_health();
+        py::dict d;
+        d["us"] = double(ms) * 1e3;
+        d["bytes"] = uint64_t(rows) * row_bytes_;
+        d["mismatched_rows"] = bad;
+        d["done_epoch"] = seen;
+        d["expected_epoch"] = epoch;
+        return d;
     }
 
     // Litmus test of the release/acquire flag protocol (between fetches only;
@@ -1044,6 +1161,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.ctas_per_sm = tuning_ctas_per_sm_;
         g.unroll = tuning_unroll_;
         g.strided = tuning_strided_;
+        g.vector_bytes = tuning_vector_;
 
         DispatchParams &d = dispatch_;
         d = DispatchParams{};
@@ -1187,6 +1305,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
     uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0, tuning_strided_ = 0;
+    uint32_t tuning_vector_ = 32;
     std::string gather_choice_ = "auto";
     // request deduplication: mode 0 off, 1 on, 2 auto (on while the last
     // measured unique ratio is below kDedupOnRatio; re-measured every
@@ -1315,6 +1434,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("write", &Runtime::write, py::arg("layer"), py::arg("storage"), py::arg("scales") = py::none())
         .def("fetch", &Runtime::fetch)
         .def("wait_layer", &Runtime::wait_layer)
+        .def("fetch_all", &Runtime::fetch_all)
         .def("check_health", &Runtime::check_health)
         .def("barrier", &Runtime::barrier)
         .def("barrier_state", &Runtime::barrier_state)
@@ -1324,6 +1444,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("run_wait_probe", &Runtime::run_wait_probe)
         .def("debug_stop_service", &Runtime::debug_stop_service)
         .def("debug_peer_copy", &Runtime::debug_peer_copy)
+        .def("debug_serve_local", &Runtime::debug_serve_local, py::arg("rows"), py::arg("worker") = "push",
+             py::arg("blocks") = 8)
         .def("debug_peer_probe", &Runtime::debug_peer_probe, py::arg("mode_even"), py::arg("mode_odd"),
              py::arg("rows"), py::arg("blocks"), py::arg("even_share_pct") = 50, py::arg("seed") = 1)
         .def("debug_litmus_reset", &Runtime::debug_litmus_reset)

@@ -196,6 +196,11 @@ class EngramBufferBase(ABC):
         return self._generation
 
     # ---------------------------------------------------------------- shared API
+    def fetch_all(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
+        """``fetch`` plus every layer hook, in layer order; returns the per-layer outputs."""
+        hooks = self.fetch(indices, num_qps=num_qps, use_tma_aligned_col_major_sf=use_tma_aligned_col_major_sf)
+        return [hook() for hook in hooks]
+
     def barrier(self):
         """Host barrier over the group (not a stream operation; never capture it)."""
         if torch.cuda.is_available() and torch.cuda.is_initialized():

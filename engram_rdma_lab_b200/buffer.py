@@ -106,6 +106,18 @@ def _gather_kernel() -> str:
     return value
 
 
+def _gather_vector() -> int:
+    """``ENGRAM_GATHER_VECTOR``: bytes per SIMT load and store, ``32`` (default) or ``16``.
+
+    32-byte (256-bit) accesses need rows of 256 bytes or more in multiples of
+    32; other row sizes use 16 bytes whatever the setting.
+    """
+    value = os.environ.get("ENGRAM_GATHER_VECTOR", "32")
+    if value not in ("16", "32"):
+        raise ValueError("ENGRAM_GATHER_VECTOR must be '16' or '32'")
+    return int(value)
+
+
 def _dedup_mode() -> int:
     """``ENGRAM_DEDUP``: ``auto`` (default), ``1`` or ``0``.
 
@@ -236,6 +248,7 @@ class EngramBuffer(EngramBufferBase):
             gather_ctas_per_sm=env_int("ENGRAM_GATHER_CTAS_PER_SM", 0, minimum=0),
             gather_unroll=env_int("ENGRAM_GATHER_UNROLL", 0, minimum=0),
             gather_strided=env_int("ENGRAM_GATHER_STRIDED", 0, minimum=0),
+            gather_vector=_gather_vector(),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),
@@ -381,6 +394,23 @@ class EngramBuffer(EngramBufferBase):
             raise
         self._input = indices
         return self._make_hooks(generation, self.runtime.wait_layer, outputs)
+
+    def fetch_all(self, indices, num_qps=0, use_tma_aligned_col_major_sf=True):
+        """``fetch(indices)`` and every layer's hook in one native call.
+
+        Returns the per-layer outputs (``data`` or ``(data, scales)``), ready
+        on the current stream like the hooks' return values.  For callers that
+        consume all layers at once it saves the host cost of one hook call per
+        layer; no hook is left outstanding.
+        """
+        self._check_fetch_args(indices, self.device, require_cuda=True, allow_pinned=True)
+        qps = num_qps or self.num_allocated_qps
+        if not 1 <= qps <= self.num_allocated_qps:
+            raise ValueError("num_qps exceeds the allocated channels")
+        self._generation += 1  # hooks of earlier fetches are superseded
+        outputs = self.runtime.fetch_all(indices, qps, bool(use_tma_aligned_col_major_sf))
+        self._input = indices
+        return list(outputs)
 
     def device_barrier(self):
         """Enqueue a device barrier over every rank of the group on the current stream.

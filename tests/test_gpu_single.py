@@ -403,3 +403,19 @@ def test_device_barrier_one_rank_and_probe():
         assert buf.error_state()["status"] == 0
     finally:
         buf.destroy()
+
+
+@pytest.mark.parametrize("egm", [False, True])
+def test_host_route_serving_on_one_gpu(egm):
+    """The push kernel and a serving hook move a request of this rank to itself, bit-exactly, epoch after epoch."""
+    entries, hidden = (5003, 5009), 256
+    buf = make_buffer(entries, hidden, 512, 8, torch.bfloat16, 0, egm)
+    try:
+        storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda", salt=3)
+        buf.write(storages)
+        for rows, worker, blocks in ((4096, "push", 8), (4096, "hook", 8), (777, "push", 148), (1, "hook", 8)):
+            r = buf.runtime.debug_serve_local(rows, worker, blocks)
+            assert r["mismatched_rows"] == 0 and r["done_epoch"] == r["expected_epoch"], r
+        assert buf.error_state()["status"] == 0
+    finally:
+        buf.destroy()
