@@ -55,7 +55,7 @@ def buffer(fp8: bool, mirror: bool):
     dtype, packs = (torch.float8_e4m3fn, 2) if fp8 else (torch.bfloat16, 0)
     sizes = EngramBuffer.get_storage_size_hint(group, ENTRIES, HIDDEN, TOKENS, EPT, dtype, packs)
     cfg = EngramBuffer.get_theoretical_config(group, len(ENTRIES), TOKENS, EPT)
-    buf = EngramBuffer(group, *sizes, True, *cfg, num_gpu_timeout_secs=20, explicitly_destroy=True)
+    buf = EngramBuffer(group, *sizes, True, *cfg, num_gpu_timeout_secs=2, explicitly_destroy=True)
     buf.set_config(ENTRIES, HIDDEN, TOKENS, EPT, dtype, packs)
     if fp8:
         storages, scales = quantized_fp8_shard(0, 1, ENTRIES, HIDDEN, packs, "cuda")

@@ -37,8 +37,8 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 from engram_rdma_lab_b200 import EngramBuffer  # noqa: E402
 
 MODES = {"pull_v4": 0, "pull_v4_deep": 1, "pull_v8": 2, "pull_ldgsts": 3, "push_v4": 4, "push_v8": 5,
-         "push_bulk": 6, "push_seq_v8": 7, "pull_seq_v8": 8}
-ROW_CASES = [("pull_v4", "pull_v4"), ("pull_v8", "pull_v8"), ("pull_ldgsts", "pull_ldgsts"), ("push_v4", "push_v4"),
+         "push_bulk": 6, "push_seq_v8": 7, "pull_seq_v8": 8, "pull_v8_l2": 9}
+ROW_CASES = [("pull_v4", "pull_v4"), ("pull_v8", "pull_v8"), ("pull_v8_l2", "pull_v8_l2"), ("pull_ldgsts", "pull_ldgsts"), ("push_v4", "push_v4"),
              ("push_v8", "push_v8"), ("push_bulk", "push_bulk"), ("push_seq_v8", "push_seq_v8"),
              ("pull_seq_v8", "pull_seq_v8"), ("pull_v8", "push_v8")]
 

@@ -425,11 +425,11 @@ def mode_async(run):
         mismatches += wrong
         bad_rounds += (wrong > 0).long()
         run.samples.append(dict(rank=run.rank, round=it, enqueue_us=host_s * 1e6))
-    pending = not torch.cuda.current_stream().query()
+    busy = not torch.cuda.current_stream().query()
     t0 = time.perf_counter()
     torch.cuda.synchronize()
-    run.meta.update(final_sync_ms=(time.perf_counter() - t0) * 1e3, pending_after_enqueue=pending,
-                    per_forward_host_syncs=0, async_check=True)
+    run.meta.update(closing_sync_ms=(time.perf_counter() - t0) * 1e3, stream_busy_after_enqueue=busy,
+                    host_syncs_per_round=0, async_check=True)
     if int(mismatches):
         raise AssertionError(f"{int(bad_rounds)} of {a.rounds} rounds differ ({int(mismatches)} values)")
 

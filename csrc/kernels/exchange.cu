@@ -12,7 +12,8 @@
 //     owner's HBM inbox through NVLink; the last CTA of a layer publishes the
 //     mailbox headers with st.release.sys.  Packing order does not matter
 //     because every entry carries its final output position.
-//   * the owner's GPU reads the rows from its host-pinned shard zero-copy and
+//   * the owner's GPU reads the rows from its host-pinned shard zero-copy (or
+//     from its HBM mirror when it keeps one) and
 //     stores them through NVLink directly into the requester's final output
 //     positions, so the hook has nothing to scatter.  A request is split into
 //     256-row chunks claimed by CAS, so push kernels launched by the owner's

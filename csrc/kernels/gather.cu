@@ -7,23 +7,26 @@
 //     NVLink 5 / NVSwitch, this rank's own shard, or this rank's replica of
 //     the hot id prefix; never host memory of another rank;
 //   * two variants, picked per buffer (ENGRAM_GATHER_KERNEL=auto|simt|bulk):
-//       - SIMT (default when every direct row is local): each warp owns an
-//         equal contiguous range of rows; one lane resolves each row and LPR
-//         lanes move it with 16-byte loads, UNROLL rows in flight per lane;
-//       - TMA (default when rows come over NVLink): one `cp.async.bulk`
+//       - SIMT (the default, "auto" and "simt"): each warp owns an equal
+//         contiguous range of rows; one lane resolves each row and LPR lanes
+//         move it with 32-byte (or 16-byte) vector loads and stores, UNROLL
+//         rows in flight per lane.  Rows from a peer's HBM mirror are plain
+//         per-thread loads through the NVLink mapping;
+//       - TMA ring (only with ENGRAM_GATHER_KERNEL=bulk): one `cp.async.bulk`
 //         (global -> shared, completing on an mbarrier) per row into an
-//         8-stage shared ring, so one producer lane keeps hundreds of rows in
-//         flight per SM without holding registers; a consumer warp streams
-//         finished stages to the final positions; two scale warps copy each
-//         tile's FP8 scales using the indices the producer left in the stage;
+//         8-stage shared ring; a consumer warp streams finished stages to the
+//         final positions; two scale warps copy each tile's FP8 scales using
+//         the indices the producer left in the stage.  For rows on the
+//         peer-HBM route its bulk copies read the peer's memory, which the
+//         project's north star rules out for the default path, so it is an
+//         opt-in for comparison;
 //   * indices may sit in pinned host memory: both variants stage them ahead
 //     with cp.async, so the PCIe latency overlaps the row copies;
 //   * route tables, layer geometry and strides are kernel parameters
 //     (__grid_constant__), so CUDA Graph replays carry them;
 //   * an out-of-range index is recorded in the error record and zero-filled,
 //     and every barrier wait is bounded; nothing traps.
-// The bulk copies are plain (non-multicast) loads; reading a peer's memory
-// this way is allowed, multicast from peer memory never appears here.
+// The bulk copies are plain (non-multicast) loads; multicast never appears here.
 #include "params.h"
 #include "ptx.cuh"
 

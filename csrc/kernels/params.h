@@ -154,7 +154,7 @@ struct PushTask {
 // both words for epoch e + 1 and only then releases done = e at the
 // requester, so a request is executed exactly once whoever runs it.
 struct ServeParams {
-    const uint8_t *table;             // this rank's host shard, mapped for this GPU
+    const uint8_t *table;             // this rank's HBM mirror if it keeps one, else its host shard (mapped)
     const uint64_t *inbox;            // this rank's inbox [world][layers][capacity]
     uint64_t *claim;                  // [world][layers]
     uint64_t *finish;                 // [world][layers]
@@ -224,6 +224,7 @@ enum ProbeMode : uint32_t {
     kProbePushBulk = 6,    // bulk copies shared -> peer global (local bulk loads feed them)
     kProbePushSeqV8 = 7,   // 32-byte stores of random local rows into consecutive peer rows
     kProbePullSeqV8 = 8,   // 32-byte loads of consecutive peer rows into consecutive local rows
+    kProbePullV8L2 = 9,    // 32-byte loads from the peer with the 256-byte L2 prefetch-size hint
 };
 
 struct PeerProbeParams {

@@ -20,6 +20,7 @@
 //   push_seq_v8         32-byte stores of random local rows into consecutive
 //                       rows of each peer's output (a staging-buffer pattern)
 //   pull_seq_v8         32-byte loads of consecutive peer rows (streaming)
+//   pull_v8_l2          32-byte loads with the .L2::256B prefetch-size hint
 // Even CTAs run `mode_even`, odd CTAs `mode_odd`, so one launch can also
 // measure pull and push sharing the links.  Diagnostics only: it overwrites
 // output regions and runs between fetches.  No reference counterpart.
@@ -84,9 +85,18 @@ __device__ __forceinline__ RowPlan plan_row(const PeerProbeParams &p, uint32_t i
     return r;
 }
 
+__device__ __forceinline__ Vec32 ld_nc_na_l2_256_v8(const void *ptr) {
+    Vec32 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
+                   "=r"(r.v[7])
+                 : "l"(ptr));
+    return r;
+}
+
 // Register path: LPR lanes per row, BYTES per lane per access, UNROLL row
 // groups in flight per lane.
-template <int BYTES, int UNROLL>
+template <int BYTES, int UNROLL, bool L2HINT = false>
 __device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint32_t hi, uint32_t warp, uint32_t warps,
                          bool seq = false) {
     const uint32_t lane = threadIdx.x % 32;
@@ -118,7 +128,7 @@ __device__ void run_regs(const PeerProbeParams &p, bool push, uint32_t lo, uint3
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
                     if (rp[u].src)
-                        v[u] = ld_nc_na_v8(rp[u].src + off);
+                        v[u] = L2HINT ? ld_nc_na_l2_256_v8(rp[u].src + off) : ld_nc_na_v8(rp[u].src + off);
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u)
                     if (rp[u].src)
@@ -286,6 +296,9 @@ __global__ void __launch_bounds__(kProbeThreads) peer_probe_kernel(const __grid_
         break;
     case kProbePullSeqV8:
         run_regs<32, 4>(p, false, lo, hi, warp, warps, true);
+        break;
+    case kProbePullV8L2:
+        run_regs<32, 4, true>(p, false, lo, hi, warp, warps);
         break;
     default:
         break;

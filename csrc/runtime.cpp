@@ -92,7 +92,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         token_ = get<std::string>(cfg, "token");
         allow_host_vmm_ = get<bool>(cfg, "allow_host_vmm");
         gather_choice_ = get<std::string>(cfg, "gather_kernel");
-        gather_variant_ = gather_choice_ == "bulk" ? kGatherBulk : kGatherSimt;
+        gather_variant_ = gather_choice_ == "bulk" ? kGatherBulk : kGatherSimt;  // "auto" and "simt": SIMT
         tuning_ctas_per_sm_ = get<uint32_t>(cfg, "gather_ctas_per_sm");
         dedup_mode_ = get<int>(cfg, "dedup");
         tuning_unroll_ = get<uint32_t>(cfg, "gather_unroll");
@@ -287,14 +287,12 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
                 serves_any_ = true;
                 serve_[p] = 1;
             }
-        if (gather_choice_ == "auto") {
-            // Remote rows favour the TMA ring (deep asynchronous queue over
-            // NVLink); purely local gathers favour 16-byte vector loads.
-            bool remote_direct = false;
-            for (uint32_t p = 0; p < world_; ++p)
-                remote_direct |= (p != rank_ && routes_[p] == kPeerHbm);
-            gather_variant_ = remote_direct ? kGatherBulk : kGatherSimt;
-        }
+        // "auto" is the SIMT kernel on every route: its vector loads from a
+        // peer's mirror are plain per-thread loads.  The TMA ring, which
+        // issues bulk copies whose source is a peer's memory, runs only when
+        // asked for by name.
+        if (gather_choice_ == "auto")
+            gather_variant_ = kGatherSimt;
         build_params();
         // Every peer imported our descriptors during its probe, which finished
         // before the probe reports were exchanged.
@@ -795,7 +793,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     double debug_peer_probe(uint32_t mode_even, uint32_t mode_odd, uint32_t rows, int blocks, uint32_t even_share_pct,
                             uint32_t seed) {
         check(connected_ && !closed_ && egm_, "the probe needs a connected buffer with the HBM mirror");
-        check(mode_even <= kProbePullSeqV8 && mode_odd <= kProbePullSeqV8 && even_share_pct <= 100, "probe mode");
+        check(mode_even <= kProbePullV8L2 && mode_odd <= kProbePullV8L2 && even_share_pct <= 100, "probe mode");
         check(row_bytes_ % 256 == 0 && row_bytes_ <= 1024, "the probe moves rows of 256, 512 or 1024 bytes");
         PeerProbeParams pp{};
         const uint64_t arena = arena_->ptr();
@@ -1184,7 +1182,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
 
         ServeParams &v = serve_params_;
         v = ServeParams{};
-        v.table = reinterpret_cast<const uint8_t *>(host_->ptr());
+        // Serving reads the HBM mirror when this owner keeps one (a pair that
+        // fell back to the host route while the mirror is on); the rows are
+        // the same bytes as the pinned host shard, which is read otherwise.
+        v.table = reinterpret_cast<const uint8_t *>(egm_ ? arena + dev_mirror_ : host_->ptr());
         v.inbox = reinterpret_cast<const uint64_t *>(arena + dev_inbox_);
         v.claim = claim_;
         v.finish = finish_;

@@ -95,10 +95,12 @@ def _hot_rows_env() -> str:
 def _gather_kernel() -> str:
     """``ENGRAM_GATHER_KERNEL``: ``auto`` (default), ``simt`` or ``bulk``.
 
-    ``simt`` moves rows with 16-byte vector loads and is fastest when every row
-    is local (HBM gather); ``bulk`` moves each row with a TMA bulk copy into a
-    shared-memory ring and is fastest when rows come from peers over NVLink.
-    ``auto`` picks ``bulk`` when any remote owner is on the peer-HBM route.
+    ``auto`` and ``simt`` run the SIMT gather: every row, local or from a
+    peer's HBM mirror, is moved with per-thread vector loads and stores.
+    ``bulk`` runs the TMA ring instead, one ``cp.async.bulk`` per row into
+    shared memory; for rows on the peer-HBM route those bulk copies read the
+    peer's memory, which the default path never does, so it is an opt-in for
+    comparison.
     """
     value = os.environ.get("ENGRAM_GATHER_KERNEL", "auto")
     if value not in ("auto", "bulk", "simt"):

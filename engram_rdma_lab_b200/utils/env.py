@@ -32,7 +32,8 @@ KNOBS = {
     "ENGRAM_EGM_ENABLE": ("0", "1 = prefer the peer-HBM route (adds an HBM mirror of the shard)"),
     "ENGRAM_WRITE_LOCAL_SF": ("= ENGRAM_EGM_ENABLE", "1 = full local FP8 scale table, 0 = each owner's rows only"),
     "ENGRAM_DEDUP": ("auto", "move each distinct row once per fetch: auto, 1 or 0"),
-    "ENGRAM_GATHER_KERNEL": ("auto", "gather variant: auto, simt (16-B loads) or bulk (TMA ring)"),
+    "ENGRAM_GATHER_KERNEL": ("auto", "gather variant: auto = simt (vector loads), or bulk (TMA ring; bulk copies "
+                                     "read peers' memory, opt-in)"),
     "ENGRAM_GATHER_CTAS_PER_SM": ("0", "SIMT grid cap per SM (0 = 2)"),
     "ENGRAM_GATHER_UNROLL": ("0", "SIMT row steps in flight for 256-byte rows (0 = 4)"),
     "ENGRAM_GATHER_STRIDED": ("0", "1 = SIMT warps stride over 32-row groups instead of equal ranges"),

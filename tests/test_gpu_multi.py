@@ -62,12 +62,16 @@ def _peer_hbm(rank, world):
 
     _setup(rank)
     entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
-    for local_sf in (False, True):
-        # First pass: the default kernel choice (the TMA ring for remote rows);
-        # second pass: 16-byte loads from the peers' mirrors.
-        os.environ["ENGRAM_GATHER_KERNEL"] = "simt" if local_sf else "auto"
+    # The default kernel (SIMT, 32-byte vectors), the SIMT kernel with 16-byte
+    # vectors, and the opted-in TMA ring, each with both scale layouts.
+    passes = [("auto", "32", False), ("simt", "16", True), ("bulk", "32", True), ("auto", "32", True)]
+    for kernel, vector, local_sf in passes:
+        os.environ["ENGRAM_GATHER_KERNEL"] = kernel
+        os.environ["ENGRAM_GATHER_VECTOR"] = vector
         buf = _buffer(entries, hidden, 512, ept, dtype, packs, egm=True, local_sf=local_sf)
-        assert buf.memory_usage()["gather_kernel"] == ("simt" if local_sf else "tma_bulk")
+        mem = buf.memory_usage()
+        assert mem["gather_kernel"] == ("tma_bulk" if kernel == "bulk" else "simt"), mem
+        assert mem["gather_vector_bytes"] == int(vector)
         info = buf.get_route_info()
         assert info["owner_routes"] == ["peer_hbm"] * world, info
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")
@@ -97,6 +101,7 @@ def _peer_hbm(rank, world):
         dist.barrier()
         buf.destroy()
     os.environ.pop("ENGRAM_GATHER_KERNEL", None)
+    os.environ.pop("ENGRAM_GATHER_VECTOR", None)
 
 
 def _host_route(rank, world):

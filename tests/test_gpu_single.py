@@ -397,7 +397,7 @@ def test_device_barrier_one_rank_and_probe():
         torch.cuda.synchronize()
         del graph
         assert buf.runtime.barrier_state() == {"count": 11, "slots": [11]}
-        for mode in range(9):  # every ProbeMode, local rows only at world size 1
+        for mode in range(10):  # every ProbeMode, local rows only at world size 1
             us = buf.runtime.debug_peer_probe(mode, mode, 4096, 148)
             assert us > 0
         assert buf.error_state()["status"] == 0
