@@ -350,10 +350,11 @@ cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream) {
-    // Serving needs enough CTAs to keep host-memory reads in flight; a rank
-    // that serves nobody only waits.
-    hook_kernel<<<p.serve ? 8 : 1, kPushThreads, 0, stream>>>(p);
+cudaError_t launch_hook_wait(const HookParams &p, int serve_ctas, cudaStream_t stream) {
+    // Serving needs enough CTAs to keep reads of the table in flight (16 keep
+    // PCIe reads of a pinned shard at its envelope; reads of an HBM mirror
+    // want one per SM); a rank that serves nobody only waits.
+    hook_kernel<<<p.serve ? (serve_ctas > 0 ? serve_ctas : 16) : 1, kPushThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

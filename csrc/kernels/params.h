@@ -201,7 +201,7 @@ struct BarrierParams {
 cudaError_t launch_gather(const GatherParams &p, int num_sms, cudaStream_t stream);
 cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream);
 cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream);
-cudaError_t launch_hook_wait(const HookParams &p, cudaStream_t stream);
+cudaError_t launch_hook_wait(const HookParams &p, int serve_ctas, cudaStream_t stream);
 cudaError_t launch_barrier(const BarrierParams &p, cudaStream_t stream);
 // 16-byte streaming copy (peer-bandwidth diagnostics).
 cudaError_t launch_stream_copy(const void *src, void *dst, uint64_t bytes, int blocks, cudaStream_t stream);

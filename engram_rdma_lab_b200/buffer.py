@@ -109,15 +109,17 @@ def _gather_kernel() -> str:
 
 
 def _gather_vector() -> int:
-    """``ENGRAM_GATHER_VECTOR``: bytes per SIMT load and store, ``32`` (default) or ``16``.
+    """``ENGRAM_GATHER_VECTOR``: bytes per SIMT load and store, ``auto`` (default), ``32`` or ``16``.
 
-    32-byte (256-bit) accesses need rows of 256 bytes or more in multiples of
-    32; other row sizes use 16 bytes whatever the setting.
+    ``auto`` picks 32-byte (256-bit) accesses when rows come over NVLink and
+    16-byte ones when every row is local.  32-byte accesses need rows of 256
+    bytes or more in multiples of 32; other row sizes use 16 bytes whatever
+    the setting.  Returns 0 for ``auto``.
     """
-    value = os.environ.get("ENGRAM_GATHER_VECTOR", "32")
-    if value not in ("16", "32"):
-        raise ValueError("ENGRAM_GATHER_VECTOR must be '16' or '32'")
-    return int(value)
+    value = os.environ.get("ENGRAM_GATHER_VECTOR", "auto")
+    if value not in ("auto", "16", "32"):
+        raise ValueError("ENGRAM_GATHER_VECTOR must be 'auto', '16' or '32'")
+    return 0 if value == "auto" else int(value)
 
 
 def _dedup_mode() -> int:

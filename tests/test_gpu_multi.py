@@ -64,14 +64,14 @@ def _peer_hbm(rank, world):
     entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
     # The default kernel (SIMT, 32-byte vectors), the SIMT kernel with 16-byte
     # vectors, and the opted-in TMA ring, each with both scale layouts.
-    passes = [("auto", "32", False), ("simt", "16", True), ("bulk", "32", True), ("auto", "32", True)]
+    passes = [("auto", "auto", False), ("simt", "16", True), ("bulk", "32", True), ("auto", "auto", True)]
     for kernel, vector, local_sf in passes:
         os.environ["ENGRAM_GATHER_KERNEL"] = kernel
         os.environ["ENGRAM_GATHER_VECTOR"] = vector
         buf = _buffer(entries, hidden, 512, ept, dtype, packs, egm=True, local_sf=local_sf)
         mem = buf.memory_usage()
         assert mem["gather_kernel"] == ("tma_bulk" if kernel == "bulk" else "simt"), mem
-        assert mem["gather_vector_bytes"] == int(vector)
+        assert mem["gather_vector_bytes"] == (32 if vector == "auto" else int(vector))
         info = buf.get_route_info()
         assert info["owner_routes"] == ["peer_hbm"] * world, info
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")

@@ -419,3 +419,35 @@ def test_host_route_serving_on_one_gpu(egm):
         assert buf.error_state()["status"] == 0
     finally:
         buf.destroy()
+
+
+def test_fetch_all_matches_hooks_and_supersedes_them():
+    entries, hidden, ept, dtype, packs = (4099, 4111), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 256, ept, dtype, packs, True)
+    try:
+        storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda", salt=2)
+        buf.write(storages, scales)
+        idx = make_indices(0, 1, entries, 256, ept, epoch=7, padding=0.05, device="cuda")
+        hooks = buf.fetch(idx)
+        for hook in hooks:
+            hook()
+        outs = buf.fetch_all(idx)
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs, salt=2)
+        with pytest.raises(RuntimeError, match="superseded"):
+            hooks[0]()
+        # Pinned host indices and graph capture take the same path.
+        host = idx.cpu().pin_memory()
+        outs = buf.fetch_all(host)
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs, salt=2)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = buf.fetch_all(idx)
+        idx.copy_(make_indices(0, 1, entries, 256, ept, epoch=8, device="cuda"))
+        graph.replay()
+        torch.cuda.synchronize()
+        check(outs, idx, entries, hidden, dtype, packs, salt=2)
+        del graph
+    finally:
+        buf.destroy()
