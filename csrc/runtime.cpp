@@ -100,6 +100,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             tuning_strided_ = get<uint32_t>(cfg, "gather_strided");
         if (cfg.contains("gather_vector"))
             tuning_vector_ = get<uint32_t>(cfg, "gather_vector");
+        if (cfg.contains("peer_transport"))
+            push_peers_ = get<std::string>(cfg, "peer_transport") == "push";
         check(tuning_vector_ == 0 || tuning_vector_ == 16 || tuning_vector_ == 32,
               "gather vector bytes must be 0 (auto), 16 or 32");
         layers_ = uint32_t(entries_.size());
@@ -279,11 +281,17 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         for (uint32_t p = 0; p < world_; ++p)
             check(selected[p] <= routes_[p], "route exceeds probed capability");
         routes_ = selected;
+        // Transport per pair: peer-HBM pairs are pulled by the requester, or
+        // (ENGRAM_PEER_TRANSPORT=push) dispatched to the owner, which pushes
+        // the rows from its HBM mirror with the host route's serving code.
+        // Both sides agreed on the same switch, so the pairs stay symmetric.
+        pushed_.assign(world_, 0);
         has_host_routes_ = false;
         serves_any_ = false;
         serve_.assign(world_, 0);
         for (uint32_t p = 0; p < world_; ++p)
-            if (p != rank_ && routes_[p] == kHostRoute) {
+            if (p != rank_ && (routes_[p] == kHostRoute || push_peers_)) {
+                pushed_[p] = 1;
                 has_host_routes_ = true;
                 serves_any_ = true;
                 serve_[p] = 1;
@@ -299,7 +307,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         // ones when every row is local (4% faster from local HBM).
         bool remote_direct = false;
         for (uint32_t p = 0; p < world_; ++p)
-            remote_direct |= (p != rank_ && routes_[p] == kPeerHbm);
+            remote_direct |= (p != rank_ && !pushed_[p]);
         vector_bytes_ = tuning_vector_ ? tuning_vector_ : (remote_direct ? 32u : 16u);
         build_params();
         // Every peer imported our descriptors during its probe, which finished
@@ -668,6 +676,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["num_sms"] = num_sms_;
         d["gather_kernel"] = gather_variant_ == kGatherSimt ? "simt" : "tma_bulk";
         d["gather_vector_bytes"] = vector_bytes_;
+        d["peer_transport"] = push_peers_ ? "push" : "pull";
         d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
         d["dedup_fetches"] = dedup_fetches_;
         d["dedup_last_unique_ratio"] = dedup_ratio_;
@@ -1123,7 +1132,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         for (uint32_t o = 0; o < world_; ++o) {
             if (o == rank_)
                 g.direct_base[o] = egm_ ? arena + dev_mirror_ : host_->ptr();
-            else if (routes_[o] == kPeerHbm)
+            else if (!pushed_[o])
                 g.direct_base[o] = peer_dev_[o]->ptr() + dev_mirror_;
             else
                 g.direct_base[o] = 0;
@@ -1178,7 +1187,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d.error = sink();
         d.layer = lt;
         for (uint32_t o = 0; o < world_; ++o) {
-            const bool host = o != rank_ && routes_[o] == kHostRoute;
+            const bool host = o != rank_ && pushed_[o];
             d.inbox_base[o] = host ? peer_dev_[o]->ptr() + dev_inbox_ : 0;
             d.header_base[o] = host ? peer_host_[o]->ptr() : 0;
         }
@@ -1201,7 +1210,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         v.headers = reinterpret_cast<const MailboxHeader *>(mailbox_->ptr());
         v.error = sink();
         for (uint32_t r = 0; r < world_; ++r) {
-            const bool serve = r != rank_ && routes_[r] == kHostRoute;
+            const bool serve = r != rank_ && pushed_[r];
             v.out_base[r] = serve ? peer_dev_[r]->ptr() + dev_output_ : 0;
             v.done_base[r] = serve ? peer_dev_[r]->ptr() + dev_done_ : 0;
             if (serve)
@@ -1393,6 +1402,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     std::vector<int> routes_;
     std::vector<std::string> mapping_errors_;
     std::vector<uint8_t> serve_;
+    std::vector<uint8_t> pushed_;  // per owner: rows arrive by owner push (host route, or push transport)
+    bool push_peers_ = false;      // ENGRAM_PEER_TRANSPORT=push
     bool probed_ = false, ready_ = false, connected_ = false, closed_ = false;
     bool has_host_routes_ = false, serves_any_ = false;
     GatherParams gather_{};

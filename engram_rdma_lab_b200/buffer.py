@@ -122,6 +122,21 @@ def _gather_vector() -> int:
     return 0 if value == "auto" else int(value)
 
 
+def _peer_transport() -> str:
+    """``ENGRAM_PEER_TRANSPORT``: how rows of peer-HBM pairs move, ``pull`` (default) or ``push``.
+
+    ``pull``: the requester's gather loads them from the owner's HBM mirror.
+    ``push``: the requester dispatches ``(row, position)`` requests to the
+    owner, whose GPU reads its HBM mirror and stores the rows into the
+    requester's output (the host route's serving code, with the mirror as the
+    source).  Every rank must use the same value.
+    """
+    value = os.environ.get("ENGRAM_PEER_TRANSPORT", "pull")
+    if value not in ("pull", "push"):
+        raise ValueError("ENGRAM_PEER_TRANSPORT must be 'pull' or 'push'")
+    return value
+
+
 def _dedup_mode() -> int:
     """``ENGRAM_DEDUP``: ``auto`` (default), ``1`` or ``0``.
 
@@ -195,8 +210,9 @@ class EngramBuffer(EngramBufferBase):
         self.num_nvlink_ranks, self.num_rdma_ranks = self.num_scaleup_ranks, self.num_scaleout_ranks
         uuid = torch.cuda.get_device_properties(self.device).uuid
         self.fabric_domain, self.fabric_error = fabric_identity(uuid, self.egm.enabled and self.num_scaleout_ranks > 1)
+        self.peer_transport = _peer_transport()
         options = (self.egm.enabled, self.local_sf, self.use_cpu_rdma_storage, self.num_gpu_bytes,
-                   self.num_rdma_storage_bytes, self.num_allocated_qps, self.qp_depth)
+                   self.num_rdma_storage_bytes, self.num_allocated_qps, self.qp_depth, self.peer_transport)
         everyone = [None] * self.num_ranks
         dist.all_gather_object(everyone, options, group=group)
         if any(o != options for o in everyone):
@@ -253,6 +269,7 @@ class EngramBuffer(EngramBufferBase):
             gather_unroll=env_int("ENGRAM_GATHER_UNROLL", 0, minimum=0),
             gather_strided=env_int("ENGRAM_GATHER_STRIDED", 0, minimum=0),
             gather_vector=_gather_vector(),
+            peer_transport=self.peer_transport,
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),

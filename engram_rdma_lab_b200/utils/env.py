@@ -39,6 +39,8 @@ KNOBS = {
     "ENGRAM_GATHER_STRIDED": ("0", "1 = SIMT warps stride over 32-row groups instead of equal ranges"),
     "ENGRAM_GATHER_VECTOR": ("auto", "SIMT bytes per load and store: auto (32 when rows come over NVLink, else 16), "
                                      "32 (256-bit, rows of 256 B and up) or 16"),
+    "ENGRAM_PEER_TRANSPORT": ("pull", "peer-HBM pairs: pull (requester loads from the owner's mirror) or push "
+                                      "(the owner pushes from its mirror after a dispatch)"),
     "ENGRAM_HOST_VMM": ("1", "host shards as CUDA-VMM HOST_NUMA allocations (else memfd + cudaHostRegister)"),
     "ENGRAM_HOT_ROWS": ("", "replicate global ids [0, H) of each layer on every rank (H or H0,H1,...)"),
     "ENGRAM_NVTX": ("0", "1 = NVTX ranges around fetch, hooks, write and owner-service launches"),

@@ -64,14 +64,19 @@ def _peer_hbm(rank, world):
     entries, hidden, ept, dtype, packs = (20011, 20021), 256, 24, torch.float8_e4m3fn, 2
     # The default kernel (SIMT, 32-byte vectors), the SIMT kernel with 16-byte
     # vectors, and the opted-in TMA ring, each with both scale layouts.
-    passes = [("auto", "auto", False), ("simt", "16", True), ("bulk", "32", True), ("auto", "auto", True)]
-    for kernel, vector, local_sf in passes:
+    # The last pass moves the peers' rows by owner push from their mirrors.
+    passes = [("auto", "auto", False, "pull"), ("simt", "16", True, "pull"), ("bulk", "32", True, "pull"),
+              ("auto", "auto", True, "pull"), ("auto", "auto", True, "push")]
+    for kernel, vector, local_sf, transport in passes:
         os.environ["ENGRAM_GATHER_KERNEL"] = kernel
         os.environ["ENGRAM_GATHER_VECTOR"] = vector
+        os.environ["ENGRAM_PEER_TRANSPORT"] = transport
         buf = _buffer(entries, hidden, 512, ept, dtype, packs, egm=True, local_sf=local_sf)
         mem = buf.memory_usage()
         assert mem["gather_kernel"] == ("tma_bulk" if kernel == "bulk" else "simt"), mem
-        assert mem["gather_vector_bytes"] == (32 if vector == "auto" else int(vector))
+        pulled = transport == "pull" and world > 1
+        assert mem["gather_vector_bytes"] == ((32 if pulled else 16) if vector == "auto" else int(vector)), mem
+        assert mem["peer_transport"] == transport and mem["has_host_routes"] == (transport == "push"), mem
         info = buf.get_route_info()
         assert info["owner_routes"] == ["peer_hbm"] * world, info
         storages, scales = pattern_shard(rank, world, entries, hidden, dtype, packs, "cuda")
@@ -100,8 +105,8 @@ def _peer_hbm(rank, world):
         del graph
         dist.barrier()
         buf.destroy()
-    os.environ.pop("ENGRAM_GATHER_KERNEL", None)
-    os.environ.pop("ENGRAM_GATHER_VECTOR", None)
+    for knob in ("ENGRAM_GATHER_KERNEL", "ENGRAM_GATHER_VECTOR", "ENGRAM_PEER_TRANSPORT"):
+        os.environ.pop(knob, None)
 
 
 def _host_route(rank, world):
