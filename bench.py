@@ -344,9 +344,9 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
 
     Every step hands ``fetch_all`` (fetch plus every layer's wait, one native
     call) the step's indices from pinned host memory, then reads token 0's rows
-    of the last layer back into pinned host memory: a 6 KB device snapshot on
-    the compute stream, copied to the host on a side stream (two snapshots in
-    rotation), so the next lookup does not wait for the copy engine.  Input paths
+    of the last layer back into pinned host memory with SM stores through its
+    device mapping (one native call on the compute stream, no copy engine), so
+    the result never queues behind the next step's index copy.  Input paths
     (``--e2e-input``):
 
     * ``copy``: step k+1's indices are copied by the copy engine into one of
@@ -368,39 +368,28 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
     base = [p.cpu() for p in pool]
     host_pool = [base[i % len(base)].clone().pin_memory() for i in range(32)]
     row = spec.ept * spec.row_bytes
-    out_host = [torch.empty(row, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    out_host = torch.empty(row, dtype=torch.uint8).pin_memory()
     packs = spec.num_sf_packs
     mode = args.e2e_input
-    copier, reader = torch.cuda.Stream(), torch.cuda.Stream()
+    copier = torch.cuda.Stream()
     dev = [torch.empty_like(pool[0]), torch.empty_like(pool[0])]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     consumed = [torch.cuda.Event(), torch.cuda.Event()]
-    snap = [torch.empty(row, dtype=torch.uint8, device="cuda") for _ in range(2)]
-    snapped = [torch.cuda.Event(), torch.cuda.Event()]
-    read = [torch.cuda.Event(), torch.cuda.Event()]
-    readback = {"step": 0}
+    from engram_rdma_lab_b200 import _native
+
+    host_write = _native.load().host_write
+    readback = {}
 
     def read_back(outs):
-        # Each step's result goes to the host: a 6 KB snapshot on the compute
-        # stream, then its D2H on a side stream, double-buffered, so the next
-        # step's lookup does not queue behind the copy engine.
+        # Each step's result goes to the host with one native call: SM stores
+        # into the pinned buffer's device mapping, ordered on the compute
+        # stream, so it never queues behind the copy engine's index copies.
         key = id(outs[-1])
         if readback.get("key") != key:
             data = outs[-1][0] if packs else outs[-1]
             readback.update(key=key, src=data[0].view(torch.uint8) if data.shape[0] else None)
-        if readback["src"] is None:
-            return
-        k = readback["step"]
-        readback["step"] = k + 1
-        b = k % 2
-        if k >= 2:
-            compute.wait_event(read[b])  # the D2H of step k-2 has read this snapshot
-        snap[b].copy_(readback["src"])
-        snapped[b].record(compute)
-        reader.wait_event(snapped[b])
-        with torch.cuda.stream(reader):
-            out_host[b].copy_(snap[b], non_blocking=True)
-            read[b].record(reader)
+        if readback["src"] is not None:
+            host_write(readback["src"], out_host, 1)
 
     def run_host(steps):
         for k in range(steps):
@@ -431,7 +420,6 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
     t0 = time.perf_counter()
     start.record(compute)
     run(args.steps)
-    compute.wait_stream(reader)  # the interval ends after the last result reached the host
     end.record(compute)
     host_s = time.perf_counter() - t0
     torch.cuda.synchronize()
@@ -460,12 +448,12 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
         "per_requester_gbs": round(per_req, 3),
         "ms_per_step": round(ms_per_step, 5),
         "h2d_bytes_per_step": int(pool[0].numel() * pool[0].element_size()),
-        "d2h_bytes_per_step": int(out_host[0].numel()),
+        "d2h_bytes_per_step": int(out_host.numel()),
         "input_path": mode,
         "host_us_per_step": round(host_us, 2),
         "index_h2d_alone_us": round(h2d_us, 2),
         "path": f"per step: {how} -> fetch_all (fetch + every layer's wait) -> D2H of the last layer's token-0 "
-                f"rows (a device snapshot, then the copy on a side stream); eager public API",
+                f"rows (SM stores into pinned host memory, engram _C.host_write); eager public API",
         "l2": "not flushed inside the interval; 32 separate pinned index tensors cycled; fresh random rows "
               "from a table larger than L2 every step",
     }

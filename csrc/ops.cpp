@@ -1,6 +1,8 @@
 // Standalone operators of the extension: the per-owner request pack (the
-// dispatch kernel aimed at caller-owned buffers), a zero-copy host read (the
-// PCIe envelope of kernels that read pinned host memory) and the NVTX switch.
+// dispatch kernel aimed at caller-owned buffers), zero-copy host reads and
+// writes by SM loads and stores through pinned memory's device mapping (the
+// PCIe envelope of kernels that read pinned host memory; small results to the
+// host without a copy engine) and the NVTX switch.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <pybind11/stl.h>
@@ -101,9 +103,32 @@ void host_read(const torch::Tensor &src, torch::Tensor &dst, int blocks) {
                "launch host read");
 }
 
+// Streams `src` (this GPU) into `dst` (pinned host memory, written in place
+// through its device mapping with 16-byte SM stores) on the current stream.
+// A device-to-host transfer that needs no copy engine: a small result can
+// leave the GPU every step without queueing behind copies of the next step's
+// inputs.  Both are contiguous with the same byte size, a multiple of 16.
+void host_write(const torch::Tensor &src, torch::Tensor &dst, int blocks) {
+    check(dst.is_cpu() && dst.is_contiguous() && src.is_cuda() && src.is_contiguous() && src.nbytes() == dst.nbytes() &&
+              src.nbytes() % 16 == 0 && blocks >= 1 && blocks <= 65535,
+          "host_write: a CUDA source and a pinned contiguous destination of the same size (16-byte multiple)");
+    cudaPointerAttributes attr{};
+    const bool mapped = cudaPointerGetAttributes(&attr, dst.data_ptr()) == cudaSuccess &&
+                        attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr;
+    if (!mapped) {
+        cudaGetLastError();
+        check(false, "host_write: the destination must be pinned (page-locked, mapped) host memory");
+    }
+    c10::cuda::CUDAGuard guard(src.get_device());
+    cudaStream_t s = at::cuda::getCurrentCUDAStream(src.get_device()).stream();
+    check_cuda(launch_stream_copy(src.data_ptr(), attr.devicePointer, uint64_t(src.nbytes()), blocks, s),
+               "launch host write");
+}
+
 } // namespace
 
 void bind_ops(py::module_ &m) {
+    m.def("host_write", &host_write, py::arg("src"), py::arg("dst"), py::arg("blocks") = 1);
     m.def("host_read", &host_read, py::arg("src"), py::arg("dst"), py::arg("blocks") = 592);
     m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),
           py::arg("packed"), py::arg("counts"), py::arg("scratch"));

@@ -1,4 +1,4 @@
-"""Single-GPU ops: per-owner request packing vs. a plain torch reference, and the zero-copy host read."""
+"""Single-GPU ops: per-owner request packing vs. a plain torch reference, and the zero-copy host read and write."""
 
 import pytest
 import torch
@@ -60,3 +60,17 @@ def test_host_read_streams_pinned_memory_into_the_gpu():
     assert torch.equal(dst.cpu(), src)
     with pytest.raises(RuntimeError, match="pinned"):
         C.host_read(src.clone(), dst, 8)  # pageable memory is refused
+
+
+def test_host_write_streams_a_gpu_tensor_into_pinned_memory():
+    from engram_rdma_lab_b200 import _native
+
+    C = _native.load()
+    for size in (16, 6144, 1 << 20):
+        src = torch.randint(0, 255, (size,), dtype=torch.uint8, device="cuda")
+        dst = torch.zeros(size, dtype=torch.uint8).pin_memory()
+        C.host_write(src, dst, 1 if size < 8192 else 64)
+        torch.cuda.synchronize()
+        assert torch.equal(dst, src.cpu())
+    with pytest.raises(RuntimeError):
+        C.host_write(src, torch.zeros(1 << 20, dtype=torch.uint8), 8)  # pageable memory is refused
