@@ -273,7 +273,7 @@ class EngramBuffer(EngramBufferBase):
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),
-            index_staging=env_flag("ENGRAM_INDEX_STAGING", False),
+            index_staging=env_flag("ENGRAM_INDEX_STAGING", True),
         )
         native = None
         with torch.cuda.device(self.device):
@@ -395,9 +395,11 @@ class EngramBuffer(EngramBufferBase):
         """Submit every layer's lookup on the current stream; return one hook per layer.
 
         ``indices`` is int32 [layers, tokens, ept] on this GPU, or in pinned
-        host memory: then the kernels read it in place over PCIe (the step's
-        H2D is fused into the lookup) and the caller keeps it unchanged until
-        the hooks' work is done, as with any non-blocking copy.
+        host memory: then the runtime copies it on its own side stream into
+        one of two device slots, so the next step's copy overlaps this step's
+        lookup (``ENGRAM_INDEX_STAGING=0``: the kernels read it in place over
+        PCIe; under CUDA graph capture they always do), and the caller keeps it
+        unchanged until the hooks' work is done, as with any non-blocking copy.
         ``num_qps`` selects how many push channels host-route owners may use
         (0 = all allocated).  ``use_tma_aligned_col_major_sf`` selects the
         column-major, 4-aligned scale layout (default) or row-major.

@@ -44,8 +44,8 @@ KNOBS = {
     "ENGRAM_HOST_VMM": ("1", "host shards as CUDA-VMM HOST_NUMA allocations (else memfd + cudaHostRegister)"),
     "ENGRAM_HOT_ROWS": ("", "replicate global ids [0, H) of each layer on every rank (H or H0,H1,...)"),
     "ENGRAM_NVTX": ("0", "1 = NVTX ranges around fetch, hooks, write and owner-service launches"),
-    "ENGRAM_INDEX_STAGING": ("0", "1 = copy pinned host indices to the GPU on a side stream (overlaps the next "
-                                  "step's H2D with this step's gather) instead of reading them in place"),
+    "ENGRAM_INDEX_STAGING": ("1", "1 = copy pinned host indices to the GPU on a side stream (overlaps the next "
+                                  "step's H2D with this step's gather); 0 = the kernels read them in place"),
 }
 
 
