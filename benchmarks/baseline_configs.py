@@ -24,8 +24,9 @@ sampled with nvidia-smi during each point.
   replica (``ENGRAM_HOT_ROWS=262144``).  The same graph without the GEMM and
   the GEMM alone are timed too.
 * ``4``  the scaling sweep: FP8 hidden 256, ept 24, 2 x 524288 rows; tokens
-  256 / 1024 / 4096 / 16384; uniform and Zipf(1.1); ours (deduplication
-  ``auto``) and the NCCL all_to_all baseline on the same points.
+  256 / 1024 / 4096 / 16384; uniform (deduplication ``auto``) and Zipf(1.1)
+  (deduplication on); ours and the NCCL all_to_all baseline on the same
+  points.
 """
 
 from __future__ import annotations
@@ -323,24 +324,33 @@ def config3(ctx, hot):
 
 
 def config4(ctx):
+    """Scaling sweep.  Each (implementation, distribution) gets its own buffer:
+    ``ENGRAM_DEDUP=auto`` decides from the fetches it has seen and re-measures
+    only every 256 fetches once it is off, so a buffer that served uniform
+    requests first would keep deduplication off for the few Zipf fetches here.
+    Zipf points run with ``ENGRAM_DEDUP=1``, what ``auto`` picks on a steady
+    Zipf stream from its first fetch."""
     entries, hidden, ept, packs = (524288, 524288), 256, 24, 2
     token_list = [int(t) for t in ctx.args.sweep_tokens.split(",")]
     cap = max(token_list)
     for impl, cls in (("ours", EngramBuffer), ("nccl_all_to_all", TorchEngramBuffer)):
-        buf = build(cls, entries, hidden, cap, ept, torch.float8_e4m3fn, packs, {"ENGRAM_EGM_ENABLE": "1"})
         for dist_name in ("uniform", "zipf"):
+            env = {"ENGRAM_EGM_ENABLE": "1", "ENGRAM_DEDUP": "1" if dist_name == "zipf" else "auto"}
+            buf = build(cls, entries, hidden, cap, ept, torch.float8_e4m3fn, packs, env)
             for tokens in token_list:
                 pool = [make_indices(ctx.rank, ctx.world, entries, tokens, ept, epoch=e + 1, distribution=dist_name,
                                      device="cuda") for e in range(4)]
                 ok = verify(buf.fetch_all(pool[0]), pool[0], entries, hidden, torch.float8_e4m3fn, packs, ctx.world)
                 nbytes = len(entries) * tokens * ept * hidden
                 extra = {"tokens": tokens, "distribution": dist_name}
+                if impl == "ours":
+                    extra["dedup"] = env["ENGRAM_DEDUP"]
                 point(ctx, "4_scaling_sweep", impl, buf, fetch_step(buf, pool), nbytes, ok, extra)
                 if impl != "ours":
                     ctx.emit({"config": "4_scaling_sweep", "impl": impl, "tokens": tokens,
                               "distribution": dist_name, "phases_last_step": buf.phase_ms()})
-        dist.barrier()
-        buf.destroy()
+            dist.barrier()
+            buf.destroy()
 
 
 def main():

@@ -189,8 +189,8 @@ class TorchEngramBuffer(EngramBufferBase):
     def _exchange(self, indices, col_major):
         """One fetch as three ``all_to_all_single`` calls with a single host sync.
 
-        1. Bucket the requests by owner with a counting placement: a one-hot
-           running count gives each request its slot inside its owner's
+        1. Bucket the requests by owner with a counting placement: a running
+           count per owner gives each request its slot inside its owner's
            bucket, so no sort runs.
         2. Exchange the per-owner counts (device), then read sent and received
            counts back together: the only host sync, needed to size the
@@ -222,8 +222,12 @@ class TorchEngramBuffer(EngramBufferBase):
         owner = owner.clamp_max(W)  # padding (and ids past the vocabulary) go to bucket W, never sent
         counts = torch.bincount(owner, minlength=W + 1)
         offsets = torch.cumsum(counts, 0) - counts
-        running = torch.nn.functional.one_hot(owner, W + 1).cumsum(0)
-        slot = offsets.index_select(0, owner) + running.gather(1, owner[:, None]).squeeze(1) - 1
+        # Running count of each owner along the requests: one row per owner,
+        # scanned along its innermost dimension (a scan down the outer one
+        # would run one thread per owner).
+        hits = owner[None, :] == torch.arange(W + 1, device=dev, dtype=torch.int64)[:, None]
+        running = hits.cumsum(1, dtype=torch.int32)
+        slot = offsets.index_select(0, owner) + running.gather(0, owner[None, :]).squeeze(0).to(torch.int64) - 1
         request = torch.empty(N, dtype=torch.int64, device=dev)
         request.index_copy_(0, slot, (layer << 32) | torch.where(valid, x.clamp_min(0) % n, torch.zeros_like(x)))
         position_of_slot = torch.empty(N, dtype=torch.int64, device=dev)
