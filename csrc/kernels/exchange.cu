@@ -205,8 +205,10 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
 // Launched by the owner service for the requests it found in the mailbox.
 // Requests another worker already finished are skipped by the claim.
 __global__ void __launch_bounds__(kPushThreads) push_kernel(const __grid_constant__ PushParams p) {
+    // CTA b starts at task b (mod the count): the CTAs spread over the
+    // requesters at once instead of all storing into one requester's links.
     for (uint32_t t = 0; t < p.num_tasks; ++t) {
-        const PushTask &task = p.tasks[t];
+        const PushTask &task = p.tasks[(t + blockIdx.x) % p.num_tasks];
         serve_request(p.s, task.requester, task.layer, task.epoch, task.rows);
     }
 }
@@ -271,7 +273,10 @@ __global__ void __launch_bounds__(kPushThreads) hook_kernel(const __grid_constan
                 refresh_board(s);
             __syncthreads();
             const uint32_t slots = s.world * s.layers;
-            for (uint32_t i = 0; i < slots; ++i) {
+            // CTA b starts at slot b (mod the slot count), so an owner's CTAs
+            // serve every requester at once rather than one after another.
+            for (uint32_t j = 0; j < slots; ++j) {
+                const uint32_t i = (j + blockIdx.x) % slots;
                 if (threadIdx.x == 0) {
                     uint64_t task = 0;
                     if ((s.serve_mask >> (i / s.layers)) & 1ull) {

@@ -415,9 +415,12 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
 template <int LPR, int VPL, int UNROLL, int VB = 16>
 cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t total = p.layers * p.rows;
-    const uint32_t groups = (total + 31) / 32;
     const uint32_t warps = kSimtThreads / 32;
-    uint32_t blocks = (groups + warps - 1) / warps;
+    // Small batches are spread over more SMs (down to 4 items per warp) so
+    // their latency is one round of row loads; large ones fill the grid cap.
+    constexpr uint32_t kMinItemsPerWarp = 4;
+    const uint32_t per_block = p.strided ? warps * 32 : warps * kMinItemsPerWarp;
+    uint32_t blocks = (total + per_block - 1) / per_block;
     const uint32_t cap = uint32_t(num_sms) * (p.ctas_per_sm ? p.ctas_per_sm : 2);
     blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
