@@ -177,3 +177,24 @@ def _state_roundtrip(rank, world, local_sf):
 @pytest.mark.parametrize("local_sf", ["0", "1"])
 def test_state_dict_roundtrip_world2(port, local_sf):
     run_ranks(_state_roundtrip, 2, port, args=(local_sf,))
+
+
+def _fetch_all_and_barrier(rank, world):
+    spec = CONFIGS["oracle"]
+    buf = _make(world, spec, torch.bfloat16, 0)
+    storages, _ = pattern_shard(rank, world, spec.entries, spec.hidden, torch.bfloat16, 0, "cpu")
+    buf.write(storages)
+    idx = make_indices(rank, world, spec.entries, spec.tokens, spec.ept, epoch=3, padding=spec.padding)
+    hooks = buf.fetch(idx)
+    for hook in hooks:
+        hook()
+    outs = buf.fetch_all(idx)  # fetch and every hook, in layer order
+    _check(outs, idx, spec, torch.bfloat16, 0)
+    with pytest.raises(RuntimeError):
+        hooks[0]()  # superseded by fetch_all
+    buf.device_barrier()  # on this group: a one-word all-reduce
+    buf.destroy()
+
+
+def test_fetch_all_and_device_barrier_gloo(port):
+    run_ranks(_fetch_all_and_barrier, 2, port)
