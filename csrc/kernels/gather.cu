@@ -27,6 +27,8 @@
 //   * an out-of-range index is recorded in the error record and zero-filled,
 //     and every barrier wait is bounded; nothing traps.
 // The bulk copies are plain (non-multicast) loads; multicast never appears here.
+#include <type_traits>
+
 #include "params.h"
 #include "ptx.cuh"
 
@@ -257,9 +259,9 @@ __global__ void __launch_bounds__(kBulkThreads) gather_bulk_kernel(const __grid_
 // 16-byte vectors of each row to LPR lanes with two shuffles per row, so the
 // per-row integer work is done by one lane instead of LPR lanes.  The next
 // kIndexAhead steps' indices are loaded before this step's rows, hiding that latency.
-template <int LPR, int VPL, int UNROLL, int VB = 16>
+template <int LPR, int VPL, int UNROLL, int VB = 16, bool L2HINT = false>
 __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __grid_constant__ GatherParams p) {
-    using V = RowVec<VB>;
+    using V = typename std::conditional<L2HINT, RowVec32L2, RowVec<VB>>::type;
     __shared__ uint64_t s_direct[kMaxRanks], s_sf[kMaxRanks];
     __shared__ int32_t s_index[kSimtThreads / 32][kIndexAhead * 32];
     __shared__ uint32_t s_entries[kMaxLayers], s_tbase[kMaxLayers], s_sfbase[kMaxLayers];
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(kSimtThreads, 2) gather_simt_kernel(const __gr
     }
 }
 
-template <int LPR, int VPL, int UNROLL, int VB = 16>
+template <int LPR, int VPL, int UNROLL, int VB = 16, bool L2HINT = false>
 cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream) {
     const uint32_t total = p.layers * p.rows;
     const uint32_t warps = kSimtThreads / 32;
@@ -425,7 +427,7 @@ cudaError_t launch_simt(const GatherParams &p, int num_sms, cudaStream_t stream)
     blocks = blocks < cap ? blocks : cap;
     if (blocks == 0)
         return cudaSuccess;
-    gather_simt_kernel<LPR, VPL, UNROLL, VB><<<blocks, kSimtThreads, 0, stream>>>(p);
+    gather_simt_kernel<LPR, VPL, UNROLL, VB, L2HINT><<<blocks, kSimtThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -434,6 +436,8 @@ cudaError_t launch_simt_any(const GatherParams &p, int num_sms, cudaStream_t str
     // 256-bit vectors: 32-byte multiples of 128 bytes and more (8 lanes per
     // 256-byte row); the 16-byte kernels serve every other row size.
     if (p.vector_bytes == 32 && p.row_bytes % 32 == 0 && vectors >= 8) {
+        if (p.l2_prefetch && vectors <= 16)
+            return launch_simt<8, 1, 4, 32, true>(p, num_sms, stream);
         if (vectors <= 16)
             return launch_simt<8, 1, 4, 32>(p, num_sms, stream);
         if (vectors <= 32)

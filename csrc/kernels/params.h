@@ -93,6 +93,7 @@ struct GatherParams {
     uint32_t unroll;              // SIMT row-steps in flight for 256-byte rows (0 = default)
     uint32_t strided;             // SIMT: 1 = warps stride over 32-row groups, 0 = equal contiguous ranges
     uint32_t vector_bytes;        // SIMT: 32 = 256-bit loads and stores where the row size allows, else 16
+    uint32_t l2_prefetch;         // SIMT, 32-byte loads of rows up to 512 B: add the 256-byte L2 prefetch-size hint
     // Request deduplication (see DedupParams): when `dedup` is set, an item whose
     // slot's elected first occurrence is another item is skipped here and
     // copied locally by the expand kernel afterwards.

@@ -85,15 +85,6 @@ __device__ __forceinline__ RowPlan plan_row(const PeerProbeParams &p, uint32_t i
     return r;
 }
 
-__device__ __forceinline__ Vec32 ld_nc_na_l2_256_v8(const void *ptr) {
-    Vec32 r;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
-                   "=r"(r.v[7])
-                 : "l"(ptr));
-    return r;
-}
-
 // Register path: LPR lanes per row, BYTES per lane per access, UNROLL row
 // groups in flight per lane.
 template <int BYTES, int UNROLL, bool L2HINT = false>

@@ -70,6 +70,24 @@ template <> struct RowVec<32> {
     static __device__ __forceinline__ void store(void *p, const T &v) { st_v8(p, v); }
 };
 
+// 32-byte read-only load with the 256-byte L2 prefetch-size hint: the L2
+// fetches the whole 256-byte block the sector belongs to.  For 256-byte rows
+// the first lane's access brings the row in; over NVLink it moved random rows
+// 2% faster in the probe (517.8 vs 507.5 GB/s per GPU at 8 GPUs).
+__device__ __forceinline__ Vec32 ld_nc_na_l2_256_v8(const void *ptr) {
+    Vec32 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
+                   "=r"(r.v[7])
+                 : "l"(ptr));
+    return r;
+}
+
+// RowVec<32> whose loads carry the 256-byte L2 prefetch-size hint.
+struct RowVec32L2 : RowVec<32> {
+    static __device__ __forceinline__ T load(const void *p) { return ld_nc_na_l2_256_v8(p); }
+};
+
 // Plain 16-byte load for memory another agent may be writing concurrently
 // (host shards under a rewrite are quiesced by write(), so .nc is safe there
 // too; this variant is kept for the inbox, which peers fill).

@@ -100,6 +100,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             tuning_strided_ = get<uint32_t>(cfg, "gather_strided");
         if (cfg.contains("gather_vector"))
             tuning_vector_ = get<uint32_t>(cfg, "gather_vector");
+        if (cfg.contains("gather_l2_prefetch"))
+            tuning_l2_prefetch_ = get<bool>(cfg, "gather_l2_prefetch");
         if (cfg.contains("peer_transport"))
             push_peers_ = get<std::string>(cfg, "peer_transport") == "push";
         check(tuning_vector_ == 0 || tuning_vector_ == 16 || tuning_vector_ == 32,
@@ -677,6 +679,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["gather_kernel"] = gather_variant_ == kGatherSimt ? "simt" : "tma_bulk";
         d["gather_vector_bytes"] = vector_bytes_;
         d["peer_transport"] = push_peers_ ? "push" : "pull";
+        d["gather_l2_prefetch"] = tuning_l2_prefetch_;
         d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
         d["dedup_fetches"] = dedup_fetches_;
         d["dedup_last_unique_ratio"] = dedup_ratio_;
@@ -1177,6 +1180,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         g.unroll = tuning_unroll_;
         g.strided = tuning_strided_;
         g.vector_bytes = vector_bytes_;
+        g.l2_prefetch = tuning_l2_prefetch_ ? 1u : 0u;
 
         DispatchParams &d = dispatch_;
         d = DispatchParams{};
@@ -1329,7 +1333,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
     uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0, tuning_strided_ = 0;
-    uint32_t tuning_vector_ = 0, vector_bytes_ = 16;  // requested (0 = auto) and chosen SIMT vector bytes
+    uint32_t tuning_vector_ = 0, vector_bytes_ = 16;
+    bool tuning_l2_prefetch_ = false;  // ENGRAM_GATHER_L2_PREFETCH  // requested (0 = auto) and chosen SIMT vector bytes
     std::string gather_choice_ = "auto";
     // request deduplication: mode 0 off, 1 on, 2 auto (on while the last
     // measured unique ratio is below kDedupOnRatio; re-measured every

@@ -270,6 +270,7 @@ class EngramBuffer(EngramBufferBase):
             gather_strided=env_int("ENGRAM_GATHER_STRIDED", 0, minimum=0),
             gather_vector=_gather_vector(),
             peer_transport=self.peer_transport,
+            gather_l2_prefetch=env_flag("ENGRAM_GATHER_L2_PREFETCH", False),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),

@@ -39,6 +39,7 @@ KNOBS = {
     "ENGRAM_GATHER_STRIDED": ("0", "1 = SIMT warps stride over 32-row groups instead of equal ranges"),
     "ENGRAM_GATHER_VECTOR": ("auto", "SIMT bytes per load and store: auto (32 when rows come over NVLink, else 16), "
                                      "32 (256-bit, rows of 256 B and up) or 16"),
+    "ENGRAM_GATHER_L2_PREFETCH": ("0", "1 = the SIMT gather's 32-byte loads carry the 256-byte L2 prefetch-size hint"),
     "ENGRAM_PEER_TRANSPORT": ("pull", "peer-HBM pairs: pull (requester loads from the owner's mirror) or push "
                                       "(the owner pushes from its mirror after a dispatch)"),
     "ENGRAM_HOST_VMM": ("1", "host shards as CUDA-VMM HOST_NUMA allocations (else memfd + cudaHostRegister)"),

@@ -451,3 +451,24 @@ def test_fetch_all_matches_hooks_and_supersedes_them():
         del graph
     finally:
         buf.destroy()
+
+
+@pytest.mark.parametrize("l2_prefetch", ["0", "1"])
+def test_simt_gather_256_bit_vectors(l2_prefetch, monkeypatch):
+    """256-bit loads and stores, with and without the 256-byte L2 prefetch-size hint, bit-exact."""
+    monkeypatch.setenv("ENGRAM_GATHER_VECTOR", "32")
+    monkeypatch.setenv("ENGRAM_GATHER_L2_PREFETCH", l2_prefetch)
+    entries, hidden, ept, dtype, packs = (8191, 8209), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 512, ept, dtype, packs, True)
+    try:
+        mem = buf.memory_usage()
+        assert mem["gather_vector_bytes"] == 32 and mem["gather_l2_prefetch"] == (l2_prefetch == "1")
+        storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda", salt=4)
+        buf.write(storages, scales)
+        for tokens in (512, 37, 1):
+            idx = make_indices(0, 1, entries, tokens, ept, epoch=tokens, padding=0.03, device="cuda")
+            outs = buf.fetch_all(idx)
+            torch.cuda.synchronize()
+            check(outs, idx, entries, hidden, dtype, packs, salt=4)
+    finally:
+        buf.destroy()
