@@ -542,8 +542,11 @@ def run_rank(args):
         raise ValueError("--egm-fail-pair names a rank outside the group")
     if args.egm_fail_pair and args.route != "peer_hbm":
         raise ValueError("--egm-fail-pair needs --route peer_hbm")
-    if not (0 <= args.requester_rank < world and 0 <= args.owner_rank < world):
-        raise ValueError("requester/owner rank outside the group")
+    # The requester and owner ranks matter only for the traffic that names them.
+    if args.traffic != "all-to-all" and not 0 <= args.requester_rank < world:
+        raise ValueError("--requester-rank outside the group")
+    if args.traffic == "single" and not 0 <= args.owner_rank < world:
+        raise ValueError("--owner-rank outside the group")
     inject_probe_failures(rank, args.egm_fail_pair)
 
     entries = [int(n) for n in args.entries.split(",")]
