@@ -12,7 +12,8 @@ JSON line per case with the median CUDA-event time and the bytes moved:
   kernels run around the gather;
 * ``push`` / ``hook``: the host route's serving code moving one request of
   ``--rows`` rows of this rank to itself, read zero-copy from the pinned host
-  shard by the push kernel (``--blocks`` CTAs) or by a serving hook kernel.
+  shard (or, with ``--mirror``, from the HBM mirror) by the push kernel
+  (``--blocks`` CTAs) or by a serving hook kernel.
 
 Run: ``python benchmarks/kernel_cases.py --case gather [--launches 20]``.  Under
 ncu, capture one launch after the warm-up ones (``-k regex:<kernel> -s 3 -c 1``).
@@ -45,6 +46,8 @@ def parse():
     p.add_argument("--launches", type=int, default=20)
     p.add_argument("--rows", type=int, default=98304, help="rows of the served request (push / hook)")
     p.add_argument("--blocks", default="8", help="push CTAs, comma-separated for a sweep")
+    p.add_argument("--mirror", action="store_true",
+                   help="push / hook: serve from the HBM mirror (ENGRAM_EGM_ENABLE=1) instead of the pinned shard")
     return p.parse_args()
 
 
@@ -100,14 +103,15 @@ def main():
                     dedup_unique_ratio=mem["dedup_last_unique_ratio"])
         print(json.dumps(line), flush=True)
     else:
-        buf = buffer(fp8=False, mirror=False)
+        buf = buffer(fp8=False, mirror=args.mirror)
+        line["source"] = "hbm_mirror" if args.mirror else "pinned_host_shard"
         for blocks in (int(b) for b in args.blocks.split(",")):
             runs = [buf.runtime.debug_serve_local(args.rows, args.case, blocks) for _ in range(args.launches)]
             bad = sum(r["mismatched_rows"] for r in runs)
             us = statistics.median(r["us"] for r in (runs[2:] if len(runs) > 4 else runs))
             nbytes = runs[0]["bytes"]
-            print(json.dumps(dict(line, blocks=blocks if args.case == "push" else 8, rows=args.rows, us=round(us, 2),
-                                  bytes=nbytes, host_read_gbs=round(nbytes / (us * 1e-6) / 1e9, 2),
+            print(json.dumps(dict(line, blocks=blocks if args.case == "push" else None, rows=args.rows,
+                                  us=round(us, 2), bytes=nbytes, gbs=round(nbytes / (us * 1e-6) / 1e9, 2),
                                   mismatched_rows=bad)), flush=True)
     buf.destroy()
     dist.destroy_process_group()
