@@ -105,6 +105,7 @@ def main():
     else:
         buf = buffer(fp8=False, mirror=args.mirror)
         line["source"] = "hbm_mirror" if args.mirror else "pinned_host_shard"
+        line["chunk_rows"] = buf.memory_usage()["serve_chunk_rows"]
         for blocks in (int(b) for b in args.blocks.split(",")):
             runs = [buf.runtime.debug_serve_local(args.rows, args.case, blocks) for _ in range(args.launches)]
             bad = sum(r["mismatched_rows"] for r in runs)

@@ -16,7 +16,7 @@
 //     from its HBM mirror when it keeps one) and
 //     stores them through NVLink directly into the requester's final output
 //     positions, so the hook has nothing to scatter.  A request is split into
-//     256-row chunks claimed by CAS, so push kernels launched by the owner's
+//     chunks (512 rows by default) claimed by CAS, so push kernels launched by the owner's
 //     CPU service and the owner's own hook kernels (which serve while they
 //     wait) share the work and no GPU spins on work only another launch does.
 //   * ids of a replicated hot prefix are never dispatched: the requester's
@@ -131,13 +131,17 @@ __device__ __forceinline__ int32_t claim_chunk(uint64_t *claim, uint64_t epoch, 
 // it copied anything.  Every thread of the CTA must call it.
 __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint64_t epoch, uint32_t rows) {
     __shared__ int32_t s_chunk;
+    // The claimed chunk's entries, staged with coalesced loads so that no row
+    // load waits behind a dependent inbox load.
+    __shared__ uint32_t s_row[kMaxServeChunkRows], s_pos[kMaxServeChunkRows];
+    constexpr uint32_t kSkip = 0xFFFFFFFFu;
     const uint32_t slot = r * s.layers + l;
     const uint32_t chunks = (rows + s.chunk_rows - 1) / s.chunk_rows;
     const uint64_t *inbox = s.inbox + uint64_t(slot) * s.capacity;
     uint8_t *out = reinterpret_cast<uint8_t *>(s.out_base[r]) + uint64_t(l) * s.capacity * s.row_bytes;
     const uint32_t vectors = s.row_bytes / 16;
     constexpr uint32_t kRowsPerStep = kPushThreads / kPushLanesPerRow;
-    constexpr int kUnroll = 4;
+    constexpr int kUnroll = 8;  // 128 rows of a chunk in flight per CTA
     const uint32_t sub = threadIdx.x / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
     bool worked = false;
     while (true) {
@@ -149,8 +153,20 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
         if (c < 0 || s.out_base[r] == 0)
             break;
         worked = true;
-        const uint32_t lo = uint32_t(c) * s.chunk_rows, hi = min(lo + s.chunk_rows, rows);
-        for (uint32_t base = lo; base < hi; base += kRowsPerStep * kUnroll) {
+        const uint32_t lo = uint32_t(c) * s.chunk_rows, n = min(lo + s.chunk_rows, rows) - lo;
+        for (uint32_t i = threadIdx.x; i < n; i += kPushThreads) {
+            const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + lo + i);
+            uint32_t row = uint32_t(entry);
+            const uint32_t pos = uint32_t(entry >> 32);
+            if (!(row < s.table_rows && pos < s.capacity)) {
+                report_error(s.error, kPushBounds, l, r, entry, s.table_rows);
+                row = kSkip;
+            }
+            s_row[i] = row;
+            s_pos[i] = pos;
+        }
+        __syncthreads();
+        for (uint32_t base = 0; base < n; base += kRowsPerStep * kUnroll) {
             const uint8_t *src[kUnroll];
             uint8_t *dst[kUnroll];
 #pragma unroll
@@ -158,15 +174,9 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
                 const uint32_t i = base + u * kRowsPerStep + sub;
                 src[u] = nullptr;
                 dst[u] = nullptr;
-                if (i < hi) {
-                    const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + i);
-                    const uint32_t row = uint32_t(entry), pos = uint32_t(entry >> 32);
-                    if (row < s.table_rows && pos < s.capacity) {
-                        src[u] = s.table + uint64_t(row) * s.row_bytes;
-                        dst[u] = out + uint64_t(pos) * s.row_bytes;
-                    } else if (vlane == 0) {
-                        report_error(s.error, kPushBounds, l, r, entry, s.table_rows);
-                    }
+                if (i < n && s_row[i] != kSkip) {
+                    src[u] = s.table + uint64_t(s_row[i]) * s.row_bytes;
+                    dst[u] = out + uint64_t(s_pos[i]) * s.row_bytes;
                 }
             }
             for (uint32_t chunk = 0; chunk < vectors; chunk += kPushLanesPerRow) {
@@ -351,11 +361,15 @@ cudaError_t launch_dispatch(const DispatchParams &p, cudaStream_t stream) {
 cudaError_t launch_push(const PushParams &p, int blocks, cudaStream_t stream) {
     if (blocks <= 0 || p.num_tasks == 0)
         return cudaSuccess;
+    if (p.s.chunk_rows == 0 || p.s.chunk_rows > kMaxServeChunkRows)
+        return cudaErrorInvalidValue;  // a chunk's entries are staged in shared memory
     push_kernel<<<blocks, kPushThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_hook_wait(const HookParams &p, int serve_ctas, cudaStream_t stream) {
+    if (p.serve && (p.s.chunk_rows == 0 || p.s.chunk_rows > kMaxServeChunkRows))
+        return cudaErrorInvalidValue;  // a chunk's entries are staged in shared memory
     // Serving needs enough CTAs to keep reads of the table in flight (16 keep
     // PCIe reads of a pinned shard at its envelope; reads of an HBM mirror
     // want one per SM); a rank that serves nobody only waits.

@@ -12,6 +12,9 @@ constexpr int kMaxRanks = 64;
 constexpr int kMaxLayers = 32;
 constexpr int kHeaderBytes = 64;
 constexpr int kMaxPushTasks = 64;
+// Largest claimable chunk of an owner-push request; the serving code stages a
+// chunk's inbox entries in shared memory.
+constexpr uint32_t kMaxServeChunkRows = 512;
 
 // Error record shared with the host through mapped pinned memory.  The first
 // failing thread wins; later failures only bump the count.
@@ -43,8 +46,8 @@ enum ErrorCode : uint32_t {
     kBarrierTimeout = 6,   // a peer never reached the device barrier
 };
 
-constexpr uint32_t kGatherBulk = 0;  // TMA bulk-copy ring (default)
-constexpr uint32_t kGatherSimt = 1;  // 16-byte vector loads
+constexpr uint32_t kGatherBulk = 0;  // TMA bulk-copy ring (opt-in)
+constexpr uint32_t kGatherSimt = 1;  // per-thread 16- or 32-byte vector loads (default)
 
 
 // Mailbox header written by a requester's GPU into the owner's host shard and

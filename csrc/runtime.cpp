@@ -52,8 +52,11 @@ namespace engram {
 
 enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
 
-// Rows per claimable unit of an owner-push request.
-constexpr uint32_t kServeChunkRows = 256;
+// Default rows per claimable unit of an owner-push request.  Every serving CTA
+// claims chunks with a CAS on one word per request, so the claims of one
+// request serialise; 512 rows per chunk halves them against 256 while a 2-GPU
+// fetch of the headline shape still splits into 192 chunks.
+constexpr uint32_t kServeChunkRows = 512;
 
 namespace {
 
@@ -104,6 +107,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             tuning_l2_prefetch_ = get<bool>(cfg, "gather_l2_prefetch");
         if (cfg.contains("peer_transport"))
             push_peers_ = get<std::string>(cfg, "peer_transport") == "push";
+        if (cfg.contains("serve_chunk_rows"))
+            serve_chunk_rows_ = get<uint32_t>(cfg, "serve_chunk_rows");
+        check(serve_chunk_rows_ >= 16 && serve_chunk_rows_ <= kMaxServeChunkRows && serve_chunk_rows_ % 16 == 0,
+              "serve chunk rows must be a multiple of 16 in [16, 512]");
         check(tuning_vector_ == 0 || tuning_vector_ == 16 || tuning_vector_ == 32,
               "gather vector bytes must be 0 (auto), 16 or 32");
         layers_ = uint32_t(entries_.size());
@@ -680,6 +687,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         d["gather_vector_bytes"] = vector_bytes_;
         d["peer_transport"] = push_peers_ ? "push" : "pull";
         d["gather_l2_prefetch"] = tuning_l2_prefetch_;
+        d["serve_chunk_rows"] = serve_chunk_rows_;
         d["dedup_mode"] = dedup_mode_ == 0 ? "off" : (dedup_mode_ == 1 ? "on" : "auto");
         d["dedup_fetches"] = dedup_fetches_;
         d["dedup_last_unique_ratio"] = dedup_ratio_;
@@ -1225,7 +1233,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         v.rank = rank_;
         v.capacity = capacity_;
         v.row_bytes = row_bytes_;
-        v.chunk_rows = kServeChunkRows;
+        v.chunk_rows = serve_chunk_rows_;
         v.table_rows = table_rows_;
     }
 
@@ -1240,7 +1248,7 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
             uint32_t chunks = 0, channels = 1;
             for (size_t i = 0; i < n; ++i) {
                 p.tasks[i] = batch[at + i];
-                chunks += (p.tasks[i].rows + kServeChunkRows - 1) / kServeChunkRows;
+                chunks += (p.tasks[i].rows + serve_chunk_rows_ - 1) / serve_chunk_rows_;
                 channels = std::max(channels, std::min(p.tasks[i].channels, 16u));
             }
             p.num_tasks = uint32_t(n);
@@ -1333,8 +1341,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
     uint64_t table_rows_ = 0, timeout_ns_ = 0;
     bool egm_ = false, local_sf_ = false, allow_host_vmm_ = true;
     uint32_t gather_variant_ = kGatherBulk, tuning_ctas_per_sm_ = 0, tuning_unroll_ = 0, tuning_strided_ = 0;
-    uint32_t tuning_vector_ = 0, vector_bytes_ = 16;
-    bool tuning_l2_prefetch_ = false;  // ENGRAM_GATHER_L2_PREFETCH  // requested (0 = auto) and chosen SIMT vector bytes
+    uint32_t tuning_vector_ = 0, vector_bytes_ = 16;  // requested (0 = auto) and chosen SIMT vector bytes
+    bool tuning_l2_prefetch_ = false;  // ENGRAM_GATHER_L2_PREFETCH
+    uint32_t serve_chunk_rows_ = kServeChunkRows;  // ENGRAM_SERVE_CHUNK_ROWS
     std::string gather_choice_ = "auto";
     // request deduplication: mode 0 off, 1 on, 2 auto (on while the last
     // measured unique ratio is below kDedupOnRatio; re-measured every

@@ -271,6 +271,7 @@ class EngramBuffer(EngramBufferBase):
             gather_vector=_gather_vector(),
             peer_transport=self.peer_transport,
             gather_l2_prefetch=env_flag("ENGRAM_GATHER_L2_PREFETCH", False),
+            serve_chunk_rows=env_int("ENGRAM_SERVE_CHUNK_ROWS", 512, minimum=16),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),

@@ -7,7 +7,7 @@ The protocol (``csrc/kernels/exchange.cu``, ``csrc/owner_service.cpp``) for one
   (``header.ready = e`` with ``rows``), and only after its hook saw
   ``done == e - 1`` (every owner released the previous epoch);
 * ``claim`` and ``finish`` hold ``(e - 1) << 32 | count``: a worker claims the
-  next 256-row chunk with a CAS that succeeds only while ``claim`` is armed for
+  next 512-row chunk with a CAS that succeeds only while ``claim`` is armed for
   ``e - 1`` and ``count < chunks`` (``claim_chunk``), copies it, then adds one
   to ``finish``; the worker whose addition completes the epoch re-arms both
   words to ``e << 32`` and releases ``done = e`` (``serve_request``);

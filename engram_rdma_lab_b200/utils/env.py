@@ -42,6 +42,8 @@ KNOBS = {
     "ENGRAM_GATHER_L2_PREFETCH": ("0", "1 = the SIMT gather's 32-byte loads carry the 256-byte L2 prefetch-size hint"),
     "ENGRAM_PEER_TRANSPORT": ("pull", "peer-HBM pairs: pull (requester loads from the owner's mirror) or push "
                                       "(the owner pushes from its mirror after a dispatch)"),
+    "ENGRAM_SERVE_CHUNK_ROWS": ("512", "rows per claimed chunk of host-route and owner-push serving (multiple of 16, "
+                                       "at most 512)"),
     "ENGRAM_HOST_VMM": ("1", "host shards as CUDA-VMM HOST_NUMA allocations (else memfd + cudaHostRegister)"),
     "ENGRAM_HOT_ROWS": ("", "replicate global ids [0, H) of each layer on every rank (H or H0,H1,...)"),
     "ENGRAM_NVTX": ("0", "1 = NVTX ranges around fetch, hooks, write and owner-service launches"),
