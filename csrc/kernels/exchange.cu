@@ -16,7 +16,7 @@
 //     from its HBM mirror when it keeps one) and
 //     stores them through NVLink directly into the requester's final output
 //     positions, so the hook has nothing to scatter.  A request is split into
-//     chunks (512 rows by default) claimed by CAS, so push kernels launched by the owner's
+//     chunks (512 rows by default) claimed by fetch-and-add, so push kernels launched by the owner's
 //     CPU service and the owner's own hook kernels (which serve while they
 //     wait) share the work and no GPU spins on work only another launch does.
 //   * ids of a replicated hot prefix are never dispatched: the requester's
@@ -111,32 +111,71 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid
 }
 
 // ------------------------------------------------------------------ serving
-// Claims the next chunk of request (r, l, epoch): -1 when the request is not
-// the one armed in `claim` or every chunk is taken.
-__device__ __forceinline__ int32_t claim_chunk(uint64_t *claim, uint64_t epoch, uint32_t chunks) {
+struct Claim {
+    int32_t chunk;     // < 0: nothing to claim
+    uint32_t epoch32;  // low 32 bits of the epoch the chunk belongs to
+    uint32_t limit;    // that epoch's chunk count
+};
+
+__device__ __forceinline__ uint32_t chunk_count(uint32_t rows, uint32_t chunk_rows) {
+    return (rows + chunk_rows - 1) / chunk_rows;
+}
+
+// Claims the next chunk of a request on `claim`.  Arms the word for `epoch`
+// (with `chunks` as its limit) if it is still armed for an earlier epoch, then
+// takes a chunk with one fetch-and-add.  A CAS claim would let only one of the
+// CTAs racing for the word succeed per L2 round trip; additions do not retry
+// and pipeline in the L2.  The returned chunk can belong to a later epoch: the
+// epoch the caller meant finished and the next one, already published, was
+// armed between the look and the addition.
+__device__ __forceinline__ Claim claim_chunk(uint64_t *claim, uint64_t epoch, uint32_t chunks, ErrorSink error,
+                                             uint32_t l, uint32_t r) {
     unsigned long long *word = reinterpret_cast<unsigned long long *>(claim);
-    unsigned long long old = atomicAdd(word, 0ull);
-    while (true) {
-        if ((old >> 32) != epoch - 1 || uint32_t(old) >= chunks)
-            return -1;
-        const unsigned long long seen = atomicCAS(word, old, old + 1);
+    const uint32_t e32 = uint32_t(epoch);
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long *>(word);
+    for (uint32_t tries = 0;; ++tries) {
+        const int32_t ahead = int32_t(uint32_t(old >> 32) - e32);
+        if (ahead > 0)
+            return {-1, 0, 0};  // a later epoch is armed: this one is done
+        if (ahead == 0)
+            break;
+        // Every failed CAS saw another worker arm the word or add to it.
+        if (tries >= kMaxServeChunks) {
+            report_error(error, kServeProtocol, l, r, old, epoch);
+            return {-1, 0, 0};
+        }
+        const unsigned long long armed = (uint64_t(e32) << 32) | (uint64_t(chunks) << 16);
+        const unsigned long long seen = atomicCAS(word, old, armed);
         if (seen == old)
-            return int32_t(uint32_t(old));
+            break;
         old = seen;
     }
+    const unsigned long long v = atomicAdd(word, 1ull);
+    const uint32_t at = uint32_t(v >> 32), limit = uint32_t(v >> 16) & 0xFFFFu, count = uint32_t(v) & 0xFFFFu;
+    if (int32_t(at - e32) < 0) {
+        report_error(error, kServeProtocol, l, r, v, epoch);  // the word went back
+        return {-1, 0, 0};
+    }
+    if (count >= limit)
+        return {-1, 0, 0};
+    return {int32_t(count), at, limit};
 }
 
 // Whole-CTA worker: copies chunks of request (r, l, epoch) from this rank's
-// host shard to the requester's output until none is left.  Returns true if
-// it copied anything.  Every thread of the CTA must call it.
+// table (HBM mirror or host shard) to the requester's output until none is
+// left.  Returns true if it copied anything.  Every thread of the CTA must
+// call it.
 __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint64_t epoch, uint32_t rows) {
     __shared__ int32_t s_chunk;
+    __shared__ uint32_t s_rows;
+    __shared__ uint64_t s_epoch;
     // The claimed chunk's entries, staged with coalesced loads so that no row
     // load waits behind a dependent inbox load.
     __shared__ uint32_t s_row[kMaxServeChunkRows], s_pos[kMaxServeChunkRows];
     constexpr uint32_t kSkip = 0xFFFFFFFFu;
+    if (s.out_base[r] == 0)
+        return false;
     const uint32_t slot = r * s.layers + l;
-    const uint32_t chunks = (rows + s.chunk_rows - 1) / s.chunk_rows;
     const uint64_t *inbox = s.inbox + uint64_t(slot) * s.capacity;
     uint8_t *out = reinterpret_cast<uint8_t *>(s.out_base[r]) + uint64_t(l) * s.capacity * s.row_bytes;
     const uint32_t vectors = s.row_bytes / 16;
@@ -145,12 +184,38 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
     const uint32_t sub = threadIdx.x / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
     bool worked = false;
     while (true) {
-        if (threadIdx.x == 0)
-            s_chunk = claim_chunk(s.claim + slot, epoch, chunks);
+        if (threadIdx.x == 0) {
+            const Claim c = claim_chunk(s.claim + slot, epoch, chunk_count(rows, s.chunk_rows), s.error, l, r);
+            int32_t chunk = c.chunk;
+            if (chunk >= 0 && c.epoch32 != uint32_t(epoch)) {
+                // A chunk of a later epoch; its header is published and cannot
+                // move on before this chunk is finished.
+                const uint64_t later = epoch + uint32_t(c.epoch32 - uint32_t(epoch));
+                const MailboxHeader *h = s.headers + slot;
+                const uint64_t ready = ld_acquire_sys_u64(&h->ready);
+                const uint32_t later_rows = *reinterpret_cast<const volatile uint32_t *>(&h->rows);
+                if (ready != later) {
+                    report_error(s.error, kServeProtocol, l, r, ready, later);
+                    chunk = -1;
+                } else {
+                    epoch = later;
+                    rows = later_rows;
+                }
+            }
+            if (chunk >= 0 && chunk_count(rows, s.chunk_rows) != c.limit) {
+                report_error(s.error, kServeProtocol, l, r, rows, c.limit);
+                chunk = -1;
+            }
+            s_chunk = chunk;
+            s_epoch = epoch;
+            s_rows = rows;
+        }
         __syncthreads();
         const int32_t c = s_chunk;
+        epoch = s_epoch;
+        rows = s_rows;
         __syncthreads();
-        if (c < 0 || s.out_base[r] == 0)
+        if (c < 0)
             break;
         worked = true;
         const uint32_t lo = uint32_t(c) * s.chunk_rows, n = min(lo + s.chunk_rows, rows) - lo;
@@ -199,9 +264,12 @@ __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint
             fence_sc_sys();
             unsigned long long *fin = reinterpret_cast<unsigned long long *>(s.finish + slot);
             const unsigned long long prev = atomicAdd(fin, 1ull);
-            if (uint32_t(prev) + 1 == chunks) {
-                // Last chunk: re-arm both words for epoch + 1, then release done.
-                *reinterpret_cast<volatile unsigned long long *>(s.claim + slot) = epoch << 32;
+            if (uint32_t(prev >> 32) != uint32_t(epoch - 1))
+                report_error(s.error, kServeProtocol, l, r, prev, epoch);
+            if (uint32_t(prev) + 1 == chunk_count(rows, s.chunk_rows)) {
+                // Last chunk: reset the finish count for epoch + 1, then
+                // release done.  The claim word is armed for epoch + 1 by the
+                // first worker that sees it published.
                 *reinterpret_cast<volatile unsigned long long *>(fin) = epoch << 32;
                 fence_sc_sys();
                 auto *done = reinterpret_cast<uint64_t *>(s.done_base[r]) + (uint64_t(l) * s.world + s.rank);
@@ -293,9 +361,12 @@ __global__ void __launch_bounds__(kPushThreads) hook_kernel(const __grid_constan
                         const uint64_t b = *reinterpret_cast<const volatile unsigned long long *>(s.board + i);
                         const uint64_t epoch = b >> 32;
                         const uint32_t rows = uint32_t(b);
+                        // Worth serving: the word is still armed for an earlier
+                        // epoch (this one needs arming) or has chunks left.
                         const uint64_t armed = *reinterpret_cast<const volatile unsigned long long *>(s.claim + i);
-                        const uint32_t chunks = (rows + s.chunk_rows - 1) / s.chunk_rows;
-                        if (epoch != 0 && rows != 0 && (armed >> 32) == epoch - 1 && uint32_t(armed) < chunks)
+                        const int32_t ahead = int32_t(uint32_t(armed >> 32) - uint32_t(epoch));
+                        const uint32_t limit = uint32_t(armed >> 16) & 0xFFFFu, count = uint32_t(armed) & 0xFFFFu;
+                        if (epoch != 0 && rows != 0 && (ahead < 0 || (ahead == 0 && count < limit)))
                             task = b;
                     }
                     s_task = task;

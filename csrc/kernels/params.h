@@ -15,6 +15,10 @@ constexpr int kMaxPushTasks = 64;
 // Largest claimable chunk of an owner-push request; the serving code stages a
 // chunk's inbox entries in shared memory.
 constexpr uint32_t kMaxServeChunkRows = 512;
+// Largest chunk count of one request: the claim word keeps the limit and the
+// claimed count in 16 bits each, with headroom above the limit for additions
+// that find every chunk taken.
+constexpr uint32_t kMaxServeChunks = 1u << 15;
 
 // Error record shared with the host through mapped pinned memory.  The first
 // failing thread wins; later failures only bump the count.
@@ -44,6 +48,7 @@ enum ErrorCode : uint32_t {
     kPushBounds = 4,       // an owner got a row id or position out of bounds
     kPipelineTimeout = 5,  // a shared-memory pipeline barrier never completed
     kBarrierTimeout = 6,   // a peer never reached the device barrier
+    kServeProtocol = 7,    // a serving claim disagreed with the mailbox header
 };
 
 constexpr uint32_t kGatherBulk = 0;  // TMA bulk-copy ring (opt-in)
@@ -152,11 +157,15 @@ struct PushTask {
 // Owner-side serving state shared by the push kernel (launched by the owner
 // service) and the hook kernel (which serves inbound requests while it waits).
 // A request (requester r, layer l, epoch e) is split into chunks of
-// `chunk_rows` rows.  Workers claim chunks with a CAS on claim[r][l] and count
-// finished chunks on finish[r][l]; both words hold ((e - 1) << 32) | count
-// while epoch e is served.  The worker that finishes the last chunk re-arms
-// both words for epoch e + 1 and only then releases done = e at the
-// requester, so a request is executed exactly once whoever runs it.
+// `chunk_rows` rows.  claim[r][l] holds (armed epoch << 32) | (chunk limit <<
+// 16) | chunks claimed: a worker that knows epoch e is published and finds the
+// word armed for an earlier epoch arms it for e by CAS; every claim is then one
+// fetch-and-add.  An addition that lands after the word was armed for a later
+// (necessarily published) epoch claims a chunk of that epoch, which the worker
+// serves with the rows from the mailbox header.  finish[r][l] holds
+// ((e - 1) << 32) | chunks finished; the worker that finishes the last chunk
+// resets it for e + 1 and only then releases done = e at the requester, so a
+// request is executed exactly once whoever runs it.
 struct ServeParams {
     const uint8_t *table;             // this rank's HBM mirror if it keeps one, else its host shard (mapped)
     const uint64_t *inbox;            // this rank's inbox [world][layers][capacity]

@@ -52,10 +52,9 @@ namespace engram {
 
 enum Route : int { kHostRoute = 0, kPeerHbm = 1 };
 
-// Default rows per claimable unit of an owner-push request.  Every serving CTA
-// claims chunks with a CAS on one word per request, so the claims of one
-// request serialise; 512 rows per chunk halves them against 256 while a 2-GPU
-// fetch of the headline shape still splits into 192 chunks.
+// Default rows per claimable unit of an owner-push request: 512 rows per chunk
+// halves the claims against 256 while a 2-GPU fetch of the headline shape
+// still splits into 192 chunks.
 constexpr uint32_t kServeChunkRows = 512;
 
 namespace {
@@ -116,6 +115,8 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         layers_ = uint32_t(entries_.size());
         row_bytes_ = hidden_ * elem_;
         capacity_ = max_tokens_ * ept_;
+        check((uint64_t(capacity_) + serve_chunk_rows_ - 1) / serve_chunk_rows_ <= kMaxServeChunks,
+              "a request can exceed 32768 serving chunks: raise ENGRAM_SERVE_CHUNK_ROWS");
         check(world_ >= 1 && world_ <= kMaxRanks, "world size out of range");
         check(layers_ >= 1 && layers_ <= kMaxLayers, "layer count out of range");
         check(rank_ < world_ && local_size_ >= 1 && world_ % local_size_ == 0 && local_rank_ == rank_ % local_size_,
@@ -880,8 +881,10 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         const uint32_t slot = rank_ * layers_;          // [requester = rank][layer 0]
         const uint32_t done_slot = 0 * world_ + rank_;  // done[layer 0][owner = rank]
         uint64_t epoch = 0;
-        check_cuda(cudaMemcpy(&epoch, claim_ + slot, 8, cudaMemcpyDeviceToHost), "read claim word");
-        epoch = (epoch >> 32) + 1;  // the claim word holds (next epoch - 1) << 32 once re-armed
+        check_cuda(cudaMemcpy(&epoch, finish_ + slot, 8, cudaMemcpyDeviceToHost), "read finish word");
+        epoch = (epoch >> 32) + 1;  // the finish word holds (next epoch - 1) << 32 once reset
+        // Claim word armed for the previous epoch with every chunk taken: the
+        // first worker arms it for `epoch`.  Finish word ready for `epoch`.
         const uint64_t armed = (epoch - 1) << 32;
         std::vector<uint64_t> entries(rows);
         std::vector<uint32_t> local_rows(rows);
@@ -1441,9 +1444,9 @@ class Runtime : public std::enable_shared_from_this<Runtime> {
         volatile ErrorRecord *e = host_error_;
         static const char *names[] = {"ok", "hook wait timed out", "index outside the vocabulary",
                                       "inbox overflow", "push bounds", "gather pipeline stalled",
-                                      "device barrier timed out"};
+                                      "device barrier timed out", "serving claim disagreed with the mailbox"};
         const uint32_t s = e->status;
-        std::string what = s < 7 ? names[s] : "unknown error";
+        std::string what = s < 8 ? names[s] : "unknown error";
         return "Engram device error: " + what + " (layer " + std::to_string(e->layer) + ", owner " +
                std::to_string(e->owner) + ", observed " + std::to_string(e->observed) + ", expected " +
                std::to_string(e->expected) + ", reports " + std::to_string(e->count) + ")";

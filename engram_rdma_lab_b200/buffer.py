@@ -137,6 +137,21 @@ def _peer_transport() -> str:
     return value
 
 
+def _serve_chunk_rows() -> int:
+    """``ENGRAM_SERVE_CHUNK_ROWS``: rows per claimed chunk when an owner serves a request (default 512).
+
+    Host-route and pushed requests are split into chunks that the owner's push
+    kernels and serving hooks claim one at a time; larger chunks mean fewer
+    claims on the request's claim word.  The serving code stages a chunk's
+    inbox entries in shared memory, so the value is a multiple of 16 in
+    [16, 512].
+    """
+    value = env_int("ENGRAM_SERVE_CHUNK_ROWS", 512, minimum=16)
+    if value > 512 or value % 16:
+        raise ValueError("ENGRAM_SERVE_CHUNK_ROWS must be a multiple of 16 in [16, 512]")
+    return value
+
+
 def _dedup_mode() -> int:
     """``ENGRAM_DEDUP``: ``auto`` (default), ``1`` or ``0``.
 
@@ -271,7 +286,7 @@ class EngramBuffer(EngramBufferBase):
             gather_vector=_gather_vector(),
             peer_transport=self.peer_transport,
             gather_l2_prefetch=env_flag("ENGRAM_GATHER_L2_PREFETCH", False),
-            serve_chunk_rows=env_int("ENGRAM_SERVE_CHUNK_ROWS", 512, minimum=16),
+            serve_chunk_rows=_serve_chunk_rows(),
             dedup=_dedup_mode(),
             nvtx=env_flag("ENGRAM_NVTX", False),
             hot_rows=list(self.hot_rows),

@@ -6,21 +6,34 @@ The protocol (``csrc/kernels/exchange.cu``, ``csrc/owner_service.cpp``) for one
 * the requester's dispatch publishes epoch ``e`` in the mailbox header
   (``header.ready = e`` with ``rows``), and only after its hook saw
   ``done == e - 1`` (every owner released the previous epoch);
-* ``claim`` and ``finish`` hold ``(e - 1) << 32 | count``: a worker claims the
-  next 512-row chunk with a CAS that succeeds only while ``claim`` is armed for
-  ``e - 1`` and ``count < chunks`` (``claim_chunk``), copies it, then adds one
-  to ``finish``; the worker whose addition completes the epoch re-arms both
-  words to ``e << 32`` and releases ``done = e`` (``serve_request``);
+* the claim word holds ``(armed epoch, chunk limit, chunks claimed)``.  A
+  worker that knows epoch ``e`` is published and finds the word armed for an
+  earlier epoch arms it for ``e`` by CAS (limit = ``e``'s chunk count, count
+  0); every claim is then one fetch-and-add (``claim_chunk``), which never
+  retries, so the claims of many CTAs pipeline in the L2 instead of queueing
+  behind one another's CAS;
+* a fetch-and-add can land after the epoch the worker meant was finished and
+  the word re-armed for the next one; it then holds a chunk of that later
+  epoch, which is already published (arming needs the header), so it serves
+  it, reading the rows from the header.  Re-arming at the last finish instead
+  (``claim="add_eager"``) lets such a late addition take a chunk of an epoch
+  that is not published yet, and the model finds runs that lose it;
+* ``finish`` holds ``(e - 1, count)``; a worker adds one per copied chunk, and
+  the one that completes the epoch resets it to ``(e, 0)`` and releases
+  ``done = e`` (``serve_request``);
 * workers are push kernels that the owner's CPU service launches for epochs it
   sees in the mailbox (``OwnerService::loop``), and the owner's own hook
   kernels, which copy the header into a board and serve whatever is armed
   while they wait (``refresh_board`` / ``hook_kernel``).
 
+``claim="cas"`` restores the earlier scheme: ``claim`` held
+``(e - 1, count)``, every claim was a CAS, and the last finisher re-armed it.
+
 :func:`run` drives that model with a seeded random scheduler in which every
 atomic step of every actor is one scheduling point, and checks the protocol's
 invariants: each chunk of each epoch is copied exactly once, ``done`` is
 released only after every chunk was copied, workers never copy for an epoch
-that is not the armed one, and the service never reports an error on a legal
+that is not published, and the service never reports an error on a legal
 run.  ``strict_service=True`` restores a service that demands consecutive
 epochs; the model finds runs where hooks finished epochs the service never
 saw, which is why the service accepts forward jumps.
@@ -44,40 +57,120 @@ class Slot:
     header_chunks: int = 0
     board_epoch: int = 0
     board_chunks: int = 0
-    claim: tuple = (0, 0)   # (armed epoch - 1, chunks claimed)
-    finish: tuple = (0, 0)  # (armed epoch - 1, chunks finished)
+    claim: tuple = (0, 0, 0)  # "add": (armed epoch, chunk limit, chunks claimed); "cas": (epoch - 1, count, 0)
+    finish: tuple = (0, 0)    # (armed epoch - 1, chunks finished)
     done: int = 0
     copies: dict = field(default_factory=dict)  # (epoch, chunk) -> times copied
+    late_claims: int = 0  # fetch-and-adds that landed on a later epoch and served it
 
 
-def _worker(slot: Slot, epoch: int, chunks: int, log):
-    """A serving worker (push kernel or hook CTA) as a generator of atomic steps."""
+def _copy_and_finish(slot: Slot, epoch: int, chunk: int, chunks: int, rearm_claim: bool):
+    """Copies one claimed chunk and counts it; the last finisher releases ``done``."""
+    yield "copy"
+    if slot.done >= epoch:
+        raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied after done")
+    if slot.header_epoch != epoch:
+        raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied while the header shows {slot.header_epoch}")
+    slot.copies[(epoch, chunk)] = slot.copies.get((epoch, chunk), 0) + 1
+    yield "finish"
+    f_armed, f_count = slot.finish
+    if f_armed != epoch - 1:
+        raise ProtocolViolation(f"finish word armed for {f_armed + 1} while epoch {epoch} finishes")
+    slot.finish = (f_armed, f_count + 1)
+    if f_count + 1 == chunks:
+        yield "rearm"
+        if rearm_claim:
+            slot.claim = (epoch, 0, 0)
+        slot.finish = (epoch, 0)
+        yield "release"
+        missing = [c for c in range(chunks) if slot.copies.get((epoch, c), 0) != 1]
+        if missing:
+            raise ProtocolViolation(f"epoch {epoch} released with chunks {missing} not copied once")
+        slot.done = epoch
+
+
+def _worker_cas(slot: Slot, epoch: int, chunks: int):
+    """The CAS scheme: claim while armed for ``epoch`` (tag ``epoch - 1``)."""
     while True:
         yield "claim"
-        armed, count = slot.claim
+        armed, count, _ = slot.claim
         if armed != epoch - 1 or count >= chunks:
             return
-        slot.claim = (armed, count + 1)  # the CAS succeeded
-        chunk = count
-        yield "copy"
-        if slot.done >= epoch:
-            raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied after done")
-        slot.copies[(epoch, chunk)] = slot.copies.get((epoch, chunk), 0) + 1
-        yield "finish"
-        f_armed, f_count = slot.finish
-        if f_armed != epoch - 1:
-            raise ProtocolViolation(f"finish word armed for {f_armed + 1} while epoch {epoch} finishes")
-        slot.finish = (f_armed, f_count + 1)
-        if f_count + 1 == chunks:
-            yield "rearm"
-            slot.claim = (epoch, 0)
-            slot.finish = (epoch, 0)
-            yield "release"
-            missing = [c for c in range(chunks) if slot.copies.get((epoch, c), 0) != 1]
-            if missing:
-                raise ProtocolViolation(f"epoch {epoch} released with chunks {missing} not copied once")
-            slot.done = epoch
-            log.append(("done", epoch))
+        slot.claim = (armed, count + 1, 0)  # the CAS succeeded
+        yield from _copy_and_finish(slot, epoch, count, chunks, rearm_claim=True)
+
+
+def _worker_add_eager(slot: Slot, epoch: int, chunks: int):
+    """Fetch-and-add on a word the last finisher re-arms (unsafe: see the module doc)."""
+    while True:
+        yield "claim_add"
+        armed, count, _ = slot.claim
+        slot.claim = (armed, count + 1, 0)
+        if armed != epoch - 1 or count >= chunks:
+            return  # an addition to a word armed for another epoch is lost
+        yield from _copy_and_finish(slot, epoch, count, chunks, rearm_claim=True)
+
+
+def _claim_add(slot: Slot, epoch: int, chunks: int):
+    """``claim_chunk``: arm for ``epoch`` if behind, then one fetch-and-add.
+
+    Returns ``(epoch', chunk, limit, chunks')`` or None; ``epoch'`` can be a
+    later epoch than ``epoch`` (a late addition), whose chunk count comes
+    from the header.
+    """
+    while True:
+        yield "arm_read"
+        armed, limit, count = slot.claim
+        if armed > epoch:
+            return None
+        if armed == epoch:
+            break
+        yield "arm_cas"
+        if slot.claim == (armed, limit, count):
+            slot.claim = (epoch, chunks, 0)
+            break
+    yield "claim_add"
+    armed, limit, count = slot.claim
+    slot.claim = (armed, limit, count + 1)
+    if armed < epoch:
+        raise ProtocolViolation(f"claim word armed for {armed} after epoch {epoch} armed it")
+    if count >= limit:
+        return None
+    if armed == epoch:
+        return armed, count, limit, chunks
+    yield "late_ready"  # a chunk of a later epoch: its rows come from the header
+    seen = slot.header_epoch
+    yield "late_rows"
+    rows = slot.header_chunks
+    if seen != armed:
+        raise ProtocolViolation(f"late claim of epoch {armed} while the header shows {seen}")
+    slot.late_claims += 1
+    return armed, count, limit, rows
+
+
+def _worker_add(slot: Slot, epoch: int, chunks: int):
+    while True:
+        got = yield from _claim_add(slot, epoch, chunks)
+        if got is None:
+            return
+        epoch, chunk, limit, chunks = got
+        if chunks != limit:
+            raise ProtocolViolation(f"epoch {epoch}: {chunks} chunks from the worker's source, limit {limit}")
+        yield from _copy_and_finish(slot, epoch, chunk, limit, rearm_claim=False)
+
+
+WORKERS = {"add": _worker_add, "add_eager": _worker_add_eager, "cas": _worker_cas}
+
+
+def _worth_serving(slot: Slot, epoch: int, chunks: int, claim: str) -> bool:
+    """The hook's look at the board and the claim word before it serves."""
+    if not epoch:
+        return False
+    if claim == "add":
+        armed, limit, count = slot.claim
+        return armed < epoch or (armed == epoch and count < limit)
+    armed, count, _ = slot.claim
+    return armed == epoch - 1 and count < chunks
 
 
 def _requester(slot: Slot, epochs: list, log):
@@ -94,7 +187,7 @@ def _requester(slot: Slot, epochs: list, log):
         yield "wait_done"
 
 
-def _service(slot: Slot, spawn, strict: bool, stop):
+def _service(slot: Slot, spawn, strict: bool, stop, worker):
     """The owner's CPU thread: polls the header and launches push workers."""
     completed = 0
     while not stop():
@@ -107,10 +200,10 @@ def _service(slot: Slot, spawn, strict: bool, stop):
         if epoch < completed or (strict and epoch != completed + 1):
             raise ProtocolViolation(f"service saw epoch {epoch} after {completed}")
         completed = epoch
-        spawn(_worker(slot, epoch, chunks, []), "push")
+        spawn(worker(slot, epoch, chunks), "push")
 
 
-def _hook(slot: Slot, spawn, stop):
+def _hook(slot: Slot, stop, claim: str):
     """The owner's hook kernel: refreshes the board and serves armed requests."""
     while not stop():
         yield "refresh_ready"
@@ -119,18 +212,19 @@ def _hook(slot: Slot, spawn, stop):
         slot.board_epoch, slot.board_chunks = epoch, slot.header_chunks  # one 64-bit board store
         yield "look"
         epoch, chunks = slot.board_epoch, slot.board_chunks
-        armed, count = slot.claim
-        if epoch and armed == epoch - 1 and count < chunks:
-            yield from _worker(slot, epoch, chunks, [])
+        if _worth_serving(slot, epoch, chunks, claim):
+            yield from WORKERS[claim](slot, epoch, chunks)
 
 
 def run(seed: int, epochs: int = 6, max_chunks: int = 4, hooks: int = 2, strict_service: bool = False,
-        service_stall: float = 0.0, max_steps: int = 200000) -> dict:
+        service_stall: float = 0.0, max_steps: int = 200000, claim: str = "add") -> dict:
     """One randomized run; raises :class:`ProtocolViolation` on a broken invariant.
 
     ``service_stall`` is the probability that the service is skipped when it
-    is picked (a CPU thread that is descheduled now and then).
+    is picked (a CPU thread that is descheduled now and then).  ``claim``
+    picks the claim scheme: ``add`` (the kernels'), ``cas`` or ``add_eager``.
     """
+    worker = WORKERS[claim]
     rng = random.Random(seed)
     slot = Slot()
     plan = [rng.randint(1, max_chunks) for _ in range(epochs)]
@@ -144,9 +238,9 @@ def run(seed: int, epochs: int = 6, max_chunks: int = 4, hooks: int = 2, strict_
         actors.append([name, gen])
 
     actors.append(["requester", _requester(slot, plan, log)])
-    actors.append(["service", _service(slot, spawn, strict_service, finished)])
+    actors.append(["service", _service(slot, spawn, strict_service, finished, worker)])
     for h in range(hooks):
-        actors.append([f"hook{h}", _hook(slot, spawn, finished)])
+        actors.append([f"hook{h}", _hook(slot, finished, claim)])
     steps = 0
     while actors:
         steps += 1
@@ -164,4 +258,4 @@ def run(seed: int, epochs: int = 6, max_chunks: int = 4, hooks: int = 2, strict_
         for chunk in range(chunks):
             if slot.copies.get((epoch, chunk), 0) != 1:
                 raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied {slot.copies.get((epoch, chunk), 0)}x")
-    return {"plan": plan, "steps": steps, "done": slot.done}
+    return {"plan": plan, "steps": steps, "done": slot.done, "late_claims": slot.late_claims}

@@ -277,3 +277,16 @@ def test_expected_random_init_matches_the_owners_tables(packs):
             assert torch.equal(got[layer][1], torch.stack(want_sf).reshape(tokens, ept * packs))
         else:
             assert got[layer][1] is None
+
+
+def test_serve_chunk_rows_knob(monkeypatch):
+    from engram_rdma_lab_b200.buffer import _serve_chunk_rows
+
+    monkeypatch.delenv("ENGRAM_SERVE_CHUNK_ROWS", raising=False)
+    assert _serve_chunk_rows() == 512
+    monkeypatch.setenv("ENGRAM_SERVE_CHUNK_ROWS", "256")
+    assert _serve_chunk_rows() == 256
+    for bad in ("8", "520", "1024", "100"):
+        monkeypatch.setenv("ENGRAM_SERVE_CHUNK_ROWS", bad)
+        with pytest.raises(ValueError):
+            _serve_chunk_rows()

@@ -6,11 +6,31 @@ import pytest
 from engram_rdma_lab_b200.protocol_model import ProtocolViolation, run
 
 
+@pytest.mark.parametrize("claim", ["add", "cas"])
 @pytest.mark.parametrize("hooks", [0, 1, 3])
-def test_every_chunk_copied_once_under_random_interleavings(hooks):
+def test_every_chunk_copied_once_under_random_interleavings(hooks, claim):
+    late = 0
     for seed in range(400):
-        result = run(seed, epochs=6, max_chunks=4, hooks=hooks, service_stall=0.5)
+        result = run(seed, epochs=6, max_chunks=4, hooks=hooks, service_stall=0.5, claim=claim)
         assert result["done"] == 6
+        late += result["late_claims"]
+    if claim == "add" and hooks:
+        # Fetch-and-adds that landed on the next epoch and served it were exercised.
+        assert late > 0
+
+
+def test_fetch_and_add_claims_need_arming_at_publication():
+    """Claiming by fetch-and-add on a word that the last finisher re-arms lets
+    a worker's final (failing) addition take chunk 0 of an epoch that is not
+    published yet; nobody serves it and the epoch never completes."""
+    failures = 0
+    for seed in range(100):
+        try:
+            run(seed, hooks=1, service_stall=0.5, claim="add_eager", max_steps=20000)
+        except ProtocolViolation as error:
+            assert "no progress" in str(error)
+            failures += 1
+    assert failures > 0
 
 
 def test_hooks_alone_serve_everything_when_the_service_stalls():
