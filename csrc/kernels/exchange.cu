@@ -36,6 +36,7 @@ namespace {
 constexpr int kDispatchThreads = 256;
 constexpr int kPushThreads = 256;
 constexpr int kPushLanesPerRow = 16;
+constexpr uint32_t kSkipRow = 0xFFFFFFFFu;  // a staged entry that failed its bounds check
 
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(const __grid_constant__ DispatchParams p) {
     __shared__ uint32_t s_last;
@@ -137,8 +138,13 @@ __device__ __forceinline__ Claim claim_chunk(uint64_t *claim, uint64_t epoch, ui
         const int32_t ahead = int32_t(uint32_t(old >> 32) - e32);
         if (ahead > 0)
             return {-1, 0, 0};  // a later epoch is armed: this one is done
-        if (ahead == 0)
+        if (ahead == 0) {
+            // Every chunk already taken: leave without adding, so the 16-bit
+            // count only grows past the limit by additions that raced.
+            if ((uint32_t(old) & 0xFFFFu) >= (uint32_t(old >> 16) & 0xFFFFu))
+                return {-1, 0, 0};
             break;
+        }
         // Every failed CAS saw another worker arm the word or add to it.
         if (tries >= kMaxServeChunks) {
             report_error(error, kServeProtocol, l, r, old, epoch);
@@ -161,123 +167,181 @@ __device__ __forceinline__ Claim claim_chunk(uint64_t *claim, uint64_t epoch, ui
     return {int32_t(count), at, limit};
 }
 
+// Stages the inbox entries of chunk `c` (row, output position) into shared
+// memory; rows or positions out of bounds are reported and skipped.  Run by
+// one warp.
+__device__ __forceinline__ void stage_chunk(const ServeParams &s, const uint64_t *inbox, uint32_t c, uint32_t rows,
+                                            uint32_t l, uint32_t r, uint32_t *s_row, uint32_t *s_pos) {
+    const uint32_t lo = c * s.chunk_rows, n = min(lo + s.chunk_rows, rows) - lo;
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x % 32; i < n; i += 32) {
+        const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + lo + i);
+        uint32_t row = uint32_t(entry);
+        const uint32_t pos = uint32_t(entry >> 32);
+        if (!(row < s.table_rows && pos < s.capacity)) {
+            report_error(s.error, kPushBounds, l, r, entry, s.table_rows);
+            row = kSkipRow;
+        }
+        s_row[i] = row;
+        s_pos[i] = pos;
+    }
+}
+
+// Counts one copied chunk of (r, l, epoch).  Its stores were issued before a
+// CTA barrier that the calling thread passed, so one cumulative system-scope
+// fence orders them before the count.  The worker whose count completes the
+// epoch resets the finish word for epoch + 1 and releases done at the
+// requester; the claim word is armed for epoch + 1 by the first worker that
+// sees it published.
+__device__ __forceinline__ void finish_chunk(const ServeParams &s, uint32_t r, uint32_t l, uint32_t slot,
+                                             uint64_t epoch, uint32_t chunks) {
+    fence_sc_sys();
+    unsigned long long *fin = reinterpret_cast<unsigned long long *>(s.finish + slot);
+    const unsigned long long prev = atomicAdd(fin, 1ull);
+    if (uint32_t(prev >> 32) != uint32_t(epoch - 1))
+        report_error(s.error, kServeProtocol, l, r, prev, epoch);
+    if (uint32_t(prev) + 1 == chunks) {
+        *reinterpret_cast<volatile unsigned long long *>(fin) = epoch << 32;
+        fence_sc_sys();
+        auto *done = reinterpret_cast<uint64_t *>(s.done_base[r]) + (uint64_t(l) * s.world + s.rank);
+        st_release_sys_u64(done, epoch);
+    }
+}
+
 // Whole-CTA worker: copies chunks of request (r, l, epoch) from this rank's
 // table (HBM mirror or host shard) to the requester's output until none is
 // left.  Returns true if it copied anything.  Every thread of the CTA must
 // call it.
+//
+// Warp 0 is the control warp: while warps 1.. copy the current chunk, it
+// counts the previously copied one (system-scope fence, finish count, done
+// release), claims the next one and stages its entries in the other shared
+// buffer.  A chunk boundary then costs one CTA barrier, so CTAs that reach
+// their boundaries at the same time (claims by fetch-and-add let them start
+// together) do not leave the link idle while each fences and claims.
 __device__ bool serve_request(const ServeParams &s, uint32_t r, uint32_t l, uint64_t epoch, uint32_t rows) {
-    __shared__ int32_t s_chunk;
+    __shared__ int32_t s_chunk[2];
     __shared__ uint32_t s_rows;
     __shared__ uint64_t s_epoch;
-    // The claimed chunk's entries, staged with coalesced loads so that no row
-    // load waits behind a dependent inbox load.
-    __shared__ uint32_t s_row[kMaxServeChunkRows], s_pos[kMaxServeChunkRows];
-    constexpr uint32_t kSkip = 0xFFFFFFFFu;
-    if (s.out_base[r] == 0)
+    __shared__ uint32_t s_row[2][kMaxServeChunkRows], s_pos[2][kMaxServeChunkRows];
+    // Published requests are never empty (epochs advance only for non-empty
+    // ones); a zero here must not arm the word with a limit of 0.
+    if (s.out_base[r] == 0 || rows == 0)
         return false;
+    // Callers run this back to back: no thread may still be reading the
+    // previous call's shared words when thread 0 writes them below.
+    __syncthreads();
     const uint32_t slot = r * s.layers + l;
     const uint64_t *inbox = s.inbox + uint64_t(slot) * s.capacity;
     uint8_t *out = reinterpret_cast<uint8_t *>(s.out_base[r]) + uint64_t(l) * s.capacity * s.row_bytes;
-    const uint32_t vectors = s.row_bytes / 16;
-    constexpr uint32_t kRowsPerStep = kPushThreads / kPushLanesPerRow;
-    constexpr int kUnroll = 8;  // 128 rows of a chunk in flight per CTA
-    const uint32_t sub = threadIdx.x / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
-    bool worked = false;
-    while (true) {
-        if (threadIdx.x == 0) {
-            const Claim c = claim_chunk(s.claim + slot, epoch, chunk_count(rows, s.chunk_rows), s.error, l, r);
-            int32_t chunk = c.chunk;
-            if (chunk >= 0 && c.epoch32 != uint32_t(epoch)) {
-                // A chunk of a later epoch; its header is published and cannot
-                // move on before this chunk is finished.
-                const uint64_t later = epoch + uint32_t(c.epoch32 - uint32_t(epoch));
-                const MailboxHeader *h = s.headers + slot;
-                const uint64_t ready = ld_acquire_sys_u64(&h->ready);
-                const uint32_t later_rows = *reinterpret_cast<const volatile uint32_t *>(&h->rows);
-                if (ready != later) {
-                    report_error(s.error, kServeProtocol, l, r, ready, later);
-                    chunk = -1;
-                } else {
-                    epoch = later;
-                    rows = later_rows;
-                }
-            }
-            if (chunk >= 0 && chunk_count(rows, s.chunk_rows) != c.limit) {
-                report_error(s.error, kServeProtocol, l, r, rows, c.limit);
+    const bool control = threadIdx.x < 32;
+    // First claim: may arm the word, or land on a later (published) epoch.
+    if (threadIdx.x == 0) {
+        const Claim c = claim_chunk(s.claim + slot, epoch, chunk_count(rows, s.chunk_rows), s.error, l, r);
+        int32_t chunk = c.chunk;
+        if (chunk >= 0 && c.epoch32 != uint32_t(epoch)) {
+            // A chunk of a later epoch; its header is published and cannot
+            // move on before this chunk is finished.
+            const uint64_t later = epoch + uint32_t(c.epoch32 - uint32_t(epoch));
+            const MailboxHeader *h = s.headers + slot;
+            const uint64_t ready = ld_acquire_sys_u64(&h->ready);
+            const uint32_t later_rows = *reinterpret_cast<const volatile uint32_t *>(&h->rows);
+            if (ready != later) {
+                report_error(s.error, kServeProtocol, l, r, ready, later);
                 chunk = -1;
+            } else {
+                epoch = later;
+                rows = later_rows;
             }
-            s_chunk = chunk;
-            s_epoch = epoch;
-            s_rows = rows;
         }
-        __syncthreads();
-        const int32_t c = s_chunk;
-        epoch = s_epoch;
-        rows = s_rows;
-        __syncthreads();
-        if (c < 0)
-            break;
-        worked = true;
-        const uint32_t lo = uint32_t(c) * s.chunk_rows, n = min(lo + s.chunk_rows, rows) - lo;
-        for (uint32_t i = threadIdx.x; i < n; i += kPushThreads) {
-            const uint64_t entry = __ldcg(reinterpret_cast<const unsigned long long *>(inbox) + lo + i);
-            uint32_t row = uint32_t(entry);
-            const uint32_t pos = uint32_t(entry >> 32);
-            if (!(row < s.table_rows && pos < s.capacity)) {
-                report_error(s.error, kPushBounds, l, r, entry, s.table_rows);
-                row = kSkip;
+        if (chunk >= 0 && chunk_count(rows, s.chunk_rows) != c.limit) {
+            report_error(s.error, kServeProtocol, l, r, rows, c.limit);
+            chunk = -1;
+        }
+        s_chunk[0] = chunk;
+        s_epoch = epoch;
+        s_rows = rows;
+    }
+    __syncthreads();
+    int32_t c = s_chunk[0];
+    epoch = s_epoch;
+    rows = s_rows;
+    if (c < 0)
+        return false;
+    const uint32_t chunks = chunk_count(rows, s.chunk_rows);
+    if (control)
+        stage_chunk(s, inbox, uint32_t(c), rows, l, r, s_row[0], s_pos[0]);
+    __syncthreads();
+
+    constexpr uint32_t kCopyThreads = kPushThreads - 32;
+    constexpr uint32_t kRowsPerStep = kCopyThreads / kPushLanesPerRow;
+    constexpr int kUnroll = 8;  // 112 rows of a chunk in flight per CTA
+    const uint32_t sub = (threadIdx.x - 32) / kPushLanesPerRow, vlane = threadIdx.x % kPushLanesPerRow;
+    const uint32_t vectors = s.row_bytes / 16;
+    uint32_t b = 0;
+    bool copied_one = false;
+    while (true) {
+        if (control) {
+            if (threadIdx.x == 0) {
+                if (copied_one)
+                    finish_chunk(s, r, l, slot, epoch, chunks);
+                // The chunk in hand is unfinished, so the word is still armed
+                // for this epoch: the addition cannot land on another one.
+                const unsigned long long v = atomicAdd(reinterpret_cast<unsigned long long *>(s.claim + slot), 1ull);
+                const uint32_t limit = uint32_t(v >> 16) & 0xFFFFu, count = uint32_t(v) & 0xFFFFu;
+                int32_t next = count < limit ? int32_t(count) : -1;
+                if (uint32_t(v >> 32) != uint32_t(epoch)) {
+                    report_error(s.error, kServeProtocol, l, r, v, epoch);
+                    next = -1;
+                }
+                s_chunk[b ^ 1] = next;
             }
-            s_row[i] = row;
-            s_pos[i] = pos;
-        }
-        __syncthreads();
-        for (uint32_t base = 0; base < n; base += kRowsPerStep * kUnroll) {
-            const uint8_t *src[kUnroll];
-            uint8_t *dst[kUnroll];
+            __syncwarp();
+            const int32_t next = *reinterpret_cast<volatile int32_t *>(&s_chunk[b ^ 1]);
+            if (next >= 0)
+                stage_chunk(s, inbox, uint32_t(next), rows, l, r, s_row[b ^ 1], s_pos[b ^ 1]);
+        } else {
+            const uint32_t lo = uint32_t(c) * s.chunk_rows, n = min(lo + s.chunk_rows, rows) - lo;
+            const uint32_t *rows_in = s_row[b], *pos_in = s_pos[b];
+            for (uint32_t base = 0; base < n; base += kRowsPerStep * kUnroll) {
+                const uint8_t *src[kUnroll];
+                uint8_t *dst[kUnroll];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const uint32_t i = base + u * kRowsPerStep + sub;
-                src[u] = nullptr;
-                dst[u] = nullptr;
-                if (i < n && s_row[i] != kSkip) {
-                    src[u] = s.table + uint64_t(s_row[i]) * s.row_bytes;
-                    dst[u] = out + uint64_t(s_pos[i]) * s.row_bytes;
+                for (int u = 0; u < kUnroll; ++u) {
+                    const uint32_t i = base + u * kRowsPerStep + sub;
+                    src[u] = nullptr;
+                    dst[u] = nullptr;
+                    if (i < n && rows_in[i] != kSkipRow) {
+                        src[u] = s.table + uint64_t(rows_in[i]) * s.row_bytes;
+                        dst[u] = out + uint64_t(pos_in[i]) * s.row_bytes;
+                    }
+                }
+                for (uint32_t chunk = 0; chunk < vectors; chunk += kPushLanesPerRow) {
+                    Vec16 buf[kUnroll];
+                    const uint32_t v = chunk + vlane;
+#pragma unroll
+                    for (int u = 0; u < kUnroll; ++u)
+                        if (src[u] != nullptr && v < vectors)
+                            buf[u] = ld_nc_na_v4(src[u] + uint64_t(v) * 16);
+#pragma unroll
+                    for (int u = 0; u < kUnroll; ++u)
+                        if (dst[u] != nullptr && v < vectors)
+                            st_v4(dst[u] + uint64_t(v) * 16, buf[u]);
                 }
             }
-            for (uint32_t chunk = 0; chunk < vectors; chunk += kPushLanesPerRow) {
-                Vec16 buf[kUnroll];
-                const uint32_t v = chunk + vlane;
-#pragma unroll
-                for (int u = 0; u < kUnroll; ++u)
-                    if (src[u] != nullptr && v < vectors)
-                        buf[u] = ld_nc_na_v4(src[u] + uint64_t(v) * 16);
-#pragma unroll
-                for (int u = 0; u < kUnroll; ++u)
-                    if (dst[u] != nullptr && v < vectors)
-                        st_v4(dst[u] + uint64_t(v) * 16, buf[u]);
-            }
         }
-        // This chunk's peer stores become visible system-wide before it counts
-        // (barrier, then one cumulative system-scope fence).
+        // Chunk c's stores are issued and the next chunk is staged.
         __syncthreads();
-        if (threadIdx.x == 0) {
-            fence_sc_sys();
-            unsigned long long *fin = reinterpret_cast<unsigned long long *>(s.finish + slot);
-            const unsigned long long prev = atomicAdd(fin, 1ull);
-            if (uint32_t(prev >> 32) != uint32_t(epoch - 1))
-                report_error(s.error, kServeProtocol, l, r, prev, epoch);
-            if (uint32_t(prev) + 1 == chunk_count(rows, s.chunk_rows)) {
-                // Last chunk: reset the finish count for epoch + 1, then
-                // release done.  The claim word is armed for epoch + 1 by the
-                // first worker that sees it published.
-                *reinterpret_cast<volatile unsigned long long *>(fin) = epoch << 32;
-                fence_sc_sys();
-                auto *done = reinterpret_cast<uint64_t *>(s.done_base[r]) + (uint64_t(l) * s.world + s.rank);
-                st_release_sys_u64(done, epoch);
-            }
-        }
+        copied_one = true;
+        const int32_t next = s_chunk[b ^ 1];
+        if (next < 0)
+            break;
+        c = next;
+        b ^= 1;
     }
-    return worked;
+    if (threadIdx.x == 0)
+        finish_chunk(s, r, l, slot, epoch, chunks);
+    return true;
 }
 
 // Launched by the owner service for the requests it found in the mailbox.

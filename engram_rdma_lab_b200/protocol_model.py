@@ -15,9 +15,13 @@ The protocol (``csrc/kernels/exchange.cu``, ``csrc/owner_service.cpp``) for one
 * a fetch-and-add can land after the epoch the worker meant was finished and
   the word re-armed for the next one; it then holds a chunk of that later
   epoch, which is already published (arming needs the header), so it serves
-  it, reading the rows from the header.  Re-arming at the last finish instead
-  (``claim="add_eager"``) lets such a late addition take a chunk of an epoch
-  that is not published yet, and the model finds runs that lose it;
+  it, reading the rows from the header.  Only a worker's first claim can land
+  like that: it claims each further chunk while it still holds an unfinished
+  one (a CTA's control warp finishes the previous chunk and claims the next
+  while the other warps copy the current one), so that epoch cannot complete.
+  Re-arming at the last finish instead (``claim="add_eager"``) lets such a
+  late addition take a chunk of an epoch that is not published yet, and the
+  model finds runs that lose it;
 * ``finish`` holds ``(e - 1, count)``; a worker adds one per copied chunk, and
   the one that completes the epoch resets it to ``(e, 0)`` and releases
   ``done = e`` (``serve_request``);
@@ -64,14 +68,17 @@ class Slot:
     late_claims: int = 0  # fetch-and-adds that landed on a later epoch and served it
 
 
-def _copy_and_finish(slot: Slot, epoch: int, chunk: int, chunks: int, rearm_claim: bool):
-    """Copies one claimed chunk and counts it; the last finisher releases ``done``."""
+def _copy(slot: Slot, epoch: int, chunk: int):
     yield "copy"
     if slot.done >= epoch:
         raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied after done")
     if slot.header_epoch != epoch:
         raise ProtocolViolation(f"chunk {chunk} of epoch {epoch} copied while the header shows {slot.header_epoch}")
     slot.copies[(epoch, chunk)] = slot.copies.get((epoch, chunk), 0) + 1
+
+
+def _finish(slot: Slot, epoch: int, chunks: int, rearm_claim: bool):
+    """Counts one copied chunk; the last finisher releases ``done``."""
     yield "finish"
     f_armed, f_count = slot.finish
     if f_armed != epoch - 1:
@@ -87,6 +94,11 @@ def _copy_and_finish(slot: Slot, epoch: int, chunk: int, chunks: int, rearm_clai
         if missing:
             raise ProtocolViolation(f"epoch {epoch} released with chunks {missing} not copied once")
         slot.done = epoch
+
+
+def _copy_and_finish(slot: Slot, epoch: int, chunk: int, chunks: int, rearm_claim: bool):
+    yield from _copy(slot, epoch, chunk)
+    yield from _finish(slot, epoch, chunks, rearm_claim)
 
 
 def _worker_cas(slot: Slot, epoch: int, chunks: int):
@@ -124,6 +136,8 @@ def _claim_add(slot: Slot, epoch: int, chunks: int):
         if armed > epoch:
             return None
         if armed == epoch:
+            if count >= limit:
+                return None  # every chunk taken: leave without adding
             break
         yield "arm_cas"
         if slot.claim == (armed, limit, count):
@@ -149,14 +163,31 @@ def _claim_add(slot: Slot, epoch: int, chunks: int):
 
 
 def _worker_add(slot: Slot, epoch: int, chunks: int):
+    """``serve_request``: the first claim may arm the word or land on a later
+    epoch; while a chunk is copied, the control warp finishes the previously
+    copied chunk and claims the next one with a plain fetch-and-add, which
+    cannot land on another epoch because the chunk in hand is unfinished."""
+    got = yield from _claim_add(slot, epoch, chunks)
+    if got is None:
+        return
+    epoch, chunk, limit, chunks = got
+    if chunks != limit:
+        raise ProtocolViolation(f"epoch {epoch}: {chunks} chunks from the worker's source, limit {limit}")
+    copied = False
     while True:
-        got = yield from _claim_add(slot, epoch, chunks)
-        if got is None:
-            return
-        epoch, chunk, limit, chunks = got
-        if chunks != limit:
-            raise ProtocolViolation(f"epoch {epoch}: {chunks} chunks from the worker's source, limit {limit}")
-        yield from _copy_and_finish(slot, epoch, chunk, limit, rearm_claim=False)
+        if copied:
+            yield from _finish(slot, epoch, limit, rearm_claim=False)
+        yield "claim_add"
+        armed, lim, count = slot.claim
+        slot.claim = (armed, lim, count + 1)
+        if armed != epoch:
+            raise ProtocolViolation(f"next claim of epoch {epoch} landed on epoch {armed}")
+        yield from _copy(slot, epoch, chunk)
+        copied = True
+        if count >= lim:
+            break
+        chunk = count
+    yield from _finish(slot, epoch, limit, rearm_claim=False)
 
 
 WORKERS = {"add": _worker_add, "add_eager": _worker_add_eager, "cas": _worker_cas}
@@ -217,41 +248,46 @@ def _hook(slot: Slot, stop, claim: str):
 
 
 def run(seed: int, epochs: int = 6, max_chunks: int = 4, hooks: int = 2, strict_service: bool = False,
-        service_stall: float = 0.0, max_steps: int = 200000, claim: str = "add") -> dict:
+        service_stall: float = 0.0, max_steps: int = 200000, claim: str = "add", add_stall: float = 0.0) -> dict:
     """One randomized run; raises :class:`ProtocolViolation` on a broken invariant.
 
     ``service_stall`` is the probability that the service is skipped when it
-    is picked (a CPU thread that is descheduled now and then).  ``claim``
-    picks the claim scheme: ``add`` (the kernels'), ``cas`` or ``add_eager``.
+    is picked (a CPU thread that is descheduled now and then).  ``add_stall``
+    is the same for a worker whose next step is its claim's fetch-and-add (an
+    atomic that is slow to reach the L2), which is what makes additions land
+    on a later epoch.  ``claim`` picks the claim scheme: ``add`` (the
+    kernels'), ``cas`` or ``add_eager``.
     """
     worker = WORKERS[claim]
     rng = random.Random(seed)
     slot = Slot()
     plan = [rng.randint(1, max_chunks) for _ in range(epochs)]
     log = []
-    actors = []  # [name, generator]
+    actors = []  # [name, generator, the step it performs when next resumed]
 
     def finished():
         return slot.done == epochs
 
     def spawn(gen, name):
-        actors.append([name, gen])
+        actors.append([name, gen, None])
 
-    actors.append(["requester", _requester(slot, plan, log)])
-    actors.append(["service", _service(slot, spawn, strict_service, finished, worker)])
+    actors.append(["requester", _requester(slot, plan, log), None])
+    actors.append(["service", _service(slot, spawn, strict_service, finished, worker), None])
     for h in range(hooks):
-        actors.append([f"hook{h}", _hook(slot, finished, claim)])
+        actors.append([f"hook{h}", _hook(slot, finished, claim), None])
     steps = 0
     while actors:
         steps += 1
         if steps > max_steps:
             raise ProtocolViolation(f"no progress after {max_steps} steps (done={slot.done}, plan={plan})")
         i = rng.randrange(len(actors))
-        name, gen = actors[i]
+        name, gen, pending = actors[i]
         if name == "service" and rng.random() < service_stall:
             continue
+        if pending == "claim_add" and rng.random() < add_stall:
+            continue
         try:
-            next(gen)
+            actors[i][2] = next(gen)
         except StopIteration:
             actors.pop(i)
     for epoch, chunks in enumerate(plan, start=1):

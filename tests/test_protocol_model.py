@@ -8,13 +8,14 @@ from engram_rdma_lab_b200.protocol_model import ProtocolViolation, run
 
 @pytest.mark.parametrize("claim", ["add", "cas"])
 @pytest.mark.parametrize("hooks", [0, 1, 3])
-def test_every_chunk_copied_once_under_random_interleavings(hooks, claim):
+@pytest.mark.parametrize("add_stall", [0.0, 0.95])
+def test_every_chunk_copied_once_under_random_interleavings(hooks, claim, add_stall):
     late = 0
     for seed in range(400):
-        result = run(seed, epochs=6, max_chunks=4, hooks=hooks, service_stall=0.5, claim=claim)
+        result = run(seed, epochs=6, max_chunks=4, hooks=hooks, service_stall=0.5, claim=claim, add_stall=add_stall)
         assert result["done"] == 6
         late += result["late_claims"]
-    if claim == "add" and hooks:
+    if claim == "add" and hooks and add_stall:
         # Fetch-and-adds that landed on the next epoch and served it were exercised.
         assert late > 0
 
