@@ -21,7 +21,7 @@ with ``capacity = max_tokens * ept`` (reference ``runtime.cpp:151-156, 519-522``
 
 from __future__ import annotations
 
-from .utils.math import align, ceil_div  # noqa: F401 - ceil_div is part of this module's helpers
+from .utils.math import align
 
 from dataclasses import dataclass, field
 
