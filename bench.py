@@ -61,6 +61,9 @@ def parse():
     p.add_argument("--e2e-input", choices=["copy", "staged", "pinned"], default="staged",
                    help="end-to-end input path: a copy-engine H2D one step ahead on a side stream, the runtime's own "
                         "staging of pinned host indices, or pinned host indices read in place by the kernels")
+    p.add_argument("--e2e-host-memory", choices=["pinned", "write-combined"], default="pinned",
+                   help="end-to-end index buffers: torch pinned memory, or EngramBuffer.pinned_indices "
+                        "(pinned, write-combined: the GPU reads it without snooping the CPU's caches)")
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--no-verify", action="store_true",
                    help="skip the bit-exact check of one fetch against the random-init tables (outside the timing)")
@@ -370,7 +373,14 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
     """
     compute = torch.cuda.current_stream()
     base = [p.cpu() for p in pool]
-    host_pool = [base[i % len(base)].clone().pin_memory() for i in range(32)]
+    if args.e2e_host_memory == "write-combined" and hasattr(buf, "pinned_indices"):
+        host_pool = []
+        for i in range(32):
+            t = buf.pinned_indices(base[0].shape[1])
+            t.copy_(base[i % len(base)])
+            host_pool.append(t)
+    else:
+        host_pool = [base[i % len(base)].clone().pin_memory() for i in range(32)]
     row = spec.ept * spec.row_bytes
     out_host = torch.empty(row, dtype=torch.uint8).pin_memory()
     packs = spec.num_sf_packs
@@ -454,6 +464,7 @@ def measure_e2e(buf, spec, pool, flush, args, rank, world, use_graph):
         "h2d_bytes_per_step": int(pool[0].numel() * pool[0].element_size()),
         "d2h_bytes_per_step": int(out_host.numel()),
         "input_path": mode,
+        "host_memory": args.e2e_host_memory,
         "host_us_per_step": round(host_us, 2),
         "index_h2d_alone_us": round(h2d_us, 2),
         "path": f"per step: {how} -> fetch_all (fetch + every layer's wait) -> D2H of the last layer's token-0 "

@@ -5,7 +5,9 @@ host route's owner push from a pinned shard) are bounded by this envelope.
 For each size, pinned host memory is moved to the GPU back to back (a) by the
 copy engine (``Tensor.copy_`` from pinned memory) and (b) by SM 16-byte loads
 through the memory's device mapping (``_C.host_read``), timed with CUDA events
-after warm-up.  One JSON line per size.
+after warm-up; then both again from write-combined pinned memory
+(``_C.alloc_pinned``, the allocation behind ``EngramBuffer.pinned_indices``).
+One JSON line per size.
 
 Run: ``python benchmarks/pcie_bandwidth.py``.
 """
@@ -46,10 +48,17 @@ def main():
         row = {"bytes": size, "copy_engine_us": round(timed_us(lambda: dst.copy_(src, non_blocking=True), iters), 1)}
         for blocks in (148, 592, 2368):
             row[f"sm_read_{blocks}_us"] = round(timed_us(lambda: C.host_read(src, dst, blocks), iters), 1)
-        best = min(v for k, v in row.items() if k.endswith("_us"))
-        row["best_gbs"] = round(size / best / 1e3, 1)
         torch.cuda.synchronize()
         assert torch.equal(dst.cpu(), src), "host_read copied wrong bytes"
+        # The same source bytes in write-combined pinned memory (_C.alloc_pinned).
+        wc = C.alloc_pinned(size, True)
+        wc.copy_(src)
+        row["copy_engine_wc_us"] = round(timed_us(lambda: dst.copy_(wc, non_blocking=True), iters), 1)
+        row["sm_read_wc_592_us"] = round(timed_us(lambda: C.host_read(wc, dst, 592), iters), 1)
+        torch.cuda.synchronize()
+        assert torch.equal(dst.cpu(), src), "write-combined copy moved wrong bytes"
+        best = min(v for k, v in row.items() if k.endswith("_us"))
+        row["best_gbs"] = round(size / best / 1e3, 1)
         print(json.dumps(row), flush=True)
 
 

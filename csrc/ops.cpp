@@ -125,9 +125,26 @@ void host_write(const torch::Tensor &src, torch::Tensor &dst, int blocks) {
                "launch host write");
 }
 
+// Pinned, device-mapped host memory as a CPU uint8 tensor that frees itself
+// (cudaFreeHost) when its storage goes.  With `write_combined` the pages are
+// write-combined: the CPU writes them without filling its caches and the
+// device reads them without snooping the CPU's caches, which is what an input
+// buffer that the host writes and the GPU reads every step wants (CPU reads of
+// it are slow).
+torch::Tensor alloc_pinned(int64_t nbytes, bool write_combined) {
+    check(nbytes > 0, "alloc_pinned: size must be positive");
+    void *ptr = nullptr;
+    const unsigned flags =
+        cudaHostAllocMapped | cudaHostAllocPortable | (write_combined ? cudaHostAllocWriteCombined : 0u);
+    check_cuda(cudaHostAlloc(&ptr, size_t(nbytes), flags), "alloc_pinned");
+    return torch::from_blob(ptr, {nbytes}, [](void *p) { cudaFreeHost(p); },
+                            torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCPU));
+}
+
 } // namespace
 
 void bind_ops(py::module_ &m) {
+    m.def("alloc_pinned", &alloc_pinned, py::arg("nbytes"), py::arg("write_combined") = true);
     m.def("host_write", &host_write, py::arg("src"), py::arg("dst"), py::arg("blocks") = 1);
     m.def("host_read", &host_read, py::arg("src"), py::arg("dst"), py::arg("blocks") = 592);
     m.def("route_pack", &route_pack, py::arg("indices"), py::arg("entries"), py::arg("world"), py::arg("owners"),

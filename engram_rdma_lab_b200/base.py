@@ -201,6 +201,18 @@ class EngramBufferBase(ABC):
         hooks = self.fetch(indices, num_qps=num_qps, use_tma_aligned_col_major_sf=use_tma_aligned_col_major_sf)
         return [hook() for hook in hooks]
 
+    def pinned_indices(self, tokens: int, write_combined: bool = True) -> torch.Tensor:
+        """An int32 host tensor ``[layers, tokens, ept]`` to pass to ``fetch`` / ``fetch_all``.
+
+        Page-locked when CUDA is available, so a fetch can take it as it is.
+        This version ignores ``write_combined``; the native buffer honours it.
+        """
+        self._ready()
+        cfg = self._config
+        if not 0 <= tokens <= cfg.max_tokens:
+            raise ValueError(f"tokens must be in [0, {cfg.max_tokens}]")
+        return torch.empty((cfg.layers, tokens, cfg.ept), dtype=torch.int32, pin_memory=torch.cuda.is_available())
+
     def barrier(self):
         """Host barrier over the group (not a stream operation; never capture it)."""
         if torch.cuda.is_available() and torch.cuda.is_initialized():

@@ -452,6 +452,28 @@ class EngramBuffer(EngramBufferBase):
         self._input = indices
         return list(outputs)
 
+    def pinned_indices(self, tokens: int, write_combined: bool = True) -> torch.Tensor:
+        """An int32 host tensor ``[layers, tokens, ept]`` for ``fetch`` / ``fetch_all`` inputs.
+
+        Page-locked and mapped into the GPU's address space, so a fetch copies
+        it (``ENGRAM_INDEX_STAGING=1``) or reads it in place without a bounce
+        through pageable memory.  With ``write_combined`` (the default) the
+        pages are write-combined: the host writes them without filling its
+        caches and the GPU reads them over PCIe without snooping the CPU's
+        caches, which suits indices the host writes every step.  Fill it with
+        sequential writes (``copy_``, numpy assignment); reading it back on the
+        CPU is slow (uncached).  The memory is freed with the tensor.
+        """
+        self._ready()
+        cfg = self._config
+        if not write_combined:
+            return super().pinned_indices(tokens, False)
+        if not 0 <= tokens <= cfg.max_tokens:
+            raise ValueError(f"tokens must be in [0, {cfg.max_tokens}]")
+        count = cfg.layers * tokens * cfg.ept
+        raw = self._C.alloc_pinned(max(count, 1) * 4, True)
+        return raw.view(torch.int32)[:count].view(cfg.layers, tokens, cfg.ept)
+
     def device_barrier(self):
         """Enqueue a device barrier over every rank of the group on the current stream.
 

@@ -291,6 +291,32 @@ def test_pinned_host_indices_read_in_place(kernel, dedup, staging, monkeypatch):
         buf.destroy()
 
 
+@pytest.mark.parametrize("staging", ["0", "1"])
+def test_write_combined_pinned_indices(staging, monkeypatch):
+    """EngramBuffer.pinned_indices: write-combined pinned memory as fetch input, staged or read in place."""
+    monkeypatch.setenv("ENGRAM_INDEX_STAGING", staging)
+    entries, hidden, ept, dtype, packs = (5003, 5009), 256, 24, torch.float8_e4m3fn, 2
+    buf = make_buffer(entries, hidden, 512, ept, dtype, packs, True)
+    try:
+        storages, scales = pattern_shard(0, 1, entries, hidden, dtype, packs, "cuda")
+        buf.write(storages, scales)
+        pool = [buf.pinned_indices(tokens) for tokens in (512, 300, 512)]
+        assert all(t.is_pinned() for t in pool)
+        with pytest.raises(ValueError):
+            buf.pinned_indices(513)
+        for k in range(6):
+            idx = make_indices(0, 1, entries, pool[k % 3].shape[1], ept, epoch=20 + k, padding=0.05)
+            torch.cuda.synchronize()  # the fetch that read this buffer three steps ago is done
+            pool[k % 3].copy_(idx)
+            outs = buf.fetch_all(pool[k % 3])
+            torch.cuda.synchronize()
+            check(outs, idx, entries, hidden, dtype, packs)
+        plain = buf.pinned_indices(64, write_combined=False)
+        assert plain.is_pinned() and plain.shape == (2, 64, ept)
+    finally:
+        buf.destroy()
+
+
 def test_pinned_host_indices_under_graph_capture():
     entries, hidden, ept = (4099, 4111), 128, 8
     buf = make_buffer(entries, hidden, 256, ept, torch.bfloat16, 0, True)

@@ -193,6 +193,12 @@ def _fetch_all_and_barrier(rank, world):
     with pytest.raises(RuntimeError):
         hooks[0]()  # superseded by fetch_all
     buf.device_barrier()  # on this group: a one-word all-reduce
+    host = buf.pinned_indices(spec.tokens)
+    assert host.shape == idx.shape and host.dtype == torch.int32
+    host.copy_(idx)
+    _check(buf.fetch_all(host), idx, spec, torch.bfloat16, 0)
+    with pytest.raises(ValueError):
+        buf.pinned_indices(spec.max_tokens + 1)
     buf.destroy()
 
 
