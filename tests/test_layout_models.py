@@ -290,3 +290,26 @@ def test_serve_chunk_rows_knob(monkeypatch):
         monkeypatch.setenv("ENGRAM_SERVE_CHUNK_ROWS", bad)
         with pytest.raises(ValueError):
             _serve_chunk_rows()
+
+
+def test_serve_chunk_limits_match_the_kernels():
+    """The Python check of ENGRAM_SERVE_CHUNK_ROWS and the CUDA limits agree."""
+    import os
+    import re
+
+    from engram_rdma_lab_b200.buffer import _serve_chunk_rows
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    text = open(os.path.join(root, "csrc", "kernels", "params.h")).read()
+    max_rows = int(re.search(r"kMaxServeChunkRows = (\d+);", text).group(1))
+    base, shift = re.search(r"kMaxServeChunks = (\d+)u? << (\d+);", text).groups()
+    max_chunks = int(base) << int(shift)
+    assert max_chunks <= 1 << 15  # 16-bit limit and count in the claim word, with headroom
+    os.environ["ENGRAM_SERVE_CHUNK_ROWS"] = str(max_rows)
+    try:
+        assert _serve_chunk_rows() == max_rows
+        os.environ["ENGRAM_SERVE_CHUNK_ROWS"] = str(max_rows + 16)
+        with pytest.raises(ValueError):
+            _serve_chunk_rows()
+    finally:
+        del os.environ["ENGRAM_SERVE_CHUNK_ROWS"]
