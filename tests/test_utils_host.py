@@ -76,3 +76,25 @@ def test_doctor_reports_without_a_gpu(capsys):
     assert set(r["knobs"]) >= {"ENGRAM_EGM_ENABLE", "ENGRAM_HOT_ROWS"}
     assert doctor.main([]) == 0
     assert "knobs:" in capsys.readouterr().out
+
+
+def test_bench_reference_arm_prints_one_unavailable_line():
+    """``bench.py --impl reference`` (the driver's reference arm) exits 0 with one JSON line on rank 0 only."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--gpus", "1", "--steps", "2",
+           "--warmup", "3"]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    out = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [line for line in out.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["unavailable"]
+    env["RANK"] = "1"
+    out = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and not out.stdout.strip()
