@@ -39,6 +39,7 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+MIN_WARMUP = 3
 BASELINE_GBS_PER_REQUESTER = 180.0  # upper end of the reference's published 175-180 GB/s/requester
 METRIC = "Engram fetch GB/s/requester and p50 fetch→hook latency, 8×B200, 4096 tok"
 
@@ -67,7 +68,11 @@ def parse():
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--no-verify", action="store_true",
                    help="skip the bit-exact check of one fetch against the random-init tables (outside the timing)")
-    return p.parse_args()
+    args = p.parse_args()
+    # Timed numbers need at least 3 warm-up steps; the JSON line reports the count that ran.
+    args.warmup_requested = args.warmup
+    args.warmup = max(args.warmup, MIN_WARMUP)
+    return args
 
 
 def unavailable_reference():
@@ -296,6 +301,7 @@ def main():
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
+            **({"warmup_requested": args.warmup_requested} if args.warmup_requested != args.warmup else {}),
             "ms_per_step": round(aligned["ms_per_step"], 5),
             "higher_is_better": True,
             "scaling": "weak",

@@ -98,3 +98,19 @@ def test_bench_reference_arm_prints_one_unavailable_line():
     env["RANK"] = "1"
     out = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=120)
     assert out.returncode == 0 and not out.stdout.strip()
+
+
+def test_bench_defaults_and_minimum_warmup(monkeypatch):
+    import importlib
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    monkeypatch.syspath_prepend(root)
+    bench = importlib.import_module("bench")
+    monkeypatch.setattr(sys, "argv", ["bench.py"])
+    args = bench.parse()
+    assert args.gpus == 1 and args.steps >= 1 and args.warmup >= 3 and args.impl == "ours"
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--warmup", "1", "--steps", "2"])
+    args = bench.parse()
+    assert args.warmup == 3 and args.warmup_requested == 1
