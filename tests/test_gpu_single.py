@@ -447,6 +447,26 @@ def test_host_route_serving_on_one_gpu(egm):
         buf.destroy()
 
 
+@pytest.mark.parametrize("egm", [False, True])
+def test_serving_with_small_chunks_many_claims(egm, monkeypatch):
+    """64-row chunks: a 4096-row request is 64 claims raced by up to 296 CTAs (and the control warps' early
+    claims of the next chunk), epoch after epoch, including a request that ends in a partial chunk."""
+    monkeypatch.setenv("ENGRAM_SERVE_CHUNK_ROWS", "64")
+    entries, hidden = (5003, 5009), 256
+    buf = make_buffer(entries, hidden, 512, 8, torch.bfloat16, 0, egm)
+    try:
+        assert buf.memory_usage()["serve_chunk_rows"] == 64
+        storages, _ = pattern_shard(0, 1, entries, hidden, torch.bfloat16, 0, "cuda", salt=5)
+        buf.write(storages)
+        for rows, worker, blocks in ((4096, "push", 296), (4096, "hook", 8), (4033, "push", 148), (65, "hook", 8),
+                                     (4096, "push", 16)):
+            r = buf.runtime.debug_serve_local(rows, worker, blocks)
+            assert r["mismatched_rows"] == 0 and r["done_epoch"] == r["expected_epoch"], r
+        assert buf.error_state()["status"] == 0
+    finally:
+        buf.destroy()
+
+
 def test_fetch_all_matches_hooks_and_supersedes_them():
     entries, hidden, ept, dtype, packs = (4099, 4111), 256, 24, torch.float8_e4m3fn, 2
     buf = make_buffer(entries, hidden, 256, ept, dtype, packs, True)
